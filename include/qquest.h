@@ -1,0 +1,253 @@
+/*
+ * qquest.h — C ABI of the B200 Quest sparse-decode kernels (libqquest.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as `void*`, allocates nothing, and returns a status code
+ * (QQ_OK = 0, negative on argument errors).  Errors detected on the device
+ * (hot buffer too small, a selected position without host backup, an index
+ * out of range, a bounded wait that ran out) are OR-ed into a caller-owned
+ * 32-bit error word (`err`, device or mapped pinned host memory) and the
+ * offending request is left unmodified; the host maps them to the same
+ * exception types the reference raises.
+ *
+ * Layouts are those of the reference (wengyinqi/QwenQuest, src/qwenquest):
+ *   page bounds   bf16 [num_layers][max_reqs][max_pages][kv_heads][head_dim][2]
+ *                 ([...][0] = min, [...][1] = max; sentinels +-bf16max)   quest.py:194-198
+ *   running min/max bf16 [num_layers][max_reqs][kv_heads][head_dim]       quest.py:200-206
+ *   counters      int32 [max_reqs]                                        quest.py:207-208
+ *   req_to_token  int32 [max_reqs][max_context_len]                       memory.py:35-37
+ *   K / V pool    [rows][kv_heads][head_dim] per layer, row 0 = padding   memory.py:96-103
+ *   hot buffer    [max_reqs * (buf + 1)][kv_heads][head_dim] per layer    coordinator.py:116-126
+ *   buffer_tokens / lru_slots int32 [num_layers][max_reqs][buf]           coordinator.py:127-131
+ *
+ * Workspace: entry points that take `workspace` need qq_workspace_bytes()
+ * bytes of device memory, zero-filled once when allocated; the kernels leave
+ * its counters at zero again when they finish.  Calls that share one
+ * workspace must be ordered on one stream.
+ */
+#ifndef QQUEST_H
+#define QQUEST_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (host) ---------------------------------------------- */
+#define QQ_OK 0
+#define QQ_ERR_INVALID (-1)     /* bad argument -> ValueError                     */
+#define QQ_ERR_UNSUPPORTED (-2) /* geometry beyond a documented limit -> ValueError */
+#define QQ_ERR_CUDA (-3)        /* a CUDA launch failed -> RuntimeError             */
+#define QQ_ERR_WORKSPACE (-4)   /* workspace too small -> ValueError                */
+
+/* ---- device error bits (OR-ed into *err) ------------------------------ */
+#define QQ_DEV_ERR_CAPACITY 1u       /* device_buffer_size too small for this top-k -> RuntimeError */
+#define QQ_DEV_ERR_NO_HOST_BACKUP 2u /* selected position without host backup -> AssertionError     */
+#define QQ_DEV_ERR_BOUNDS 4u         /* an index out of range was skipped -> RuntimeError            */
+#define QQ_DEV_ERR_TIMEOUT 8u        /* a bounded wait ran out -> RuntimeError                       */
+
+/* ---- dtypes ----------------------------------------------------------- */
+#define QQ_BF16 0
+#define QQ_F32 1
+
+/* ---- limits ----------------------------------------------------------- */
+#define QQ_MAX_LAYERS 128  /* per-layer pointers travel inside the kernel parameters */
+#define QQ_MAX_BS 4096     /* requests per call                                       */
+#define QQ_MAX_CHANNELS 1024 /* kv_heads * head_dim                                   */
+
+/* Quest state of QuestAlgorithm.init_storage (quest.py:171-209). */
+typedef struct qq_quest_state {
+  uint16_t* page_bounds;
+  uint16_t* running_min;
+  uint16_t* running_max;
+  int32_t* running_token_count;
+  int32_t* running_page_idx;
+  int32_t num_layers;
+  int32_t max_reqs;
+  int32_t max_pages;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t page_size;
+  int32_t top_k;
+  int32_t avoid_recent_overlap;
+} qq_quest_state;
+
+/* The decode batch of ForwardBatch (batch.py:38-64). */
+typedef struct qq_batch {
+  const int64_t* req_pool_indices; /* device [bs] */
+  const int64_t* seq_lens;         /* device [bs]; counts the token being decoded */
+  int32_t bs;
+} qq_batch;
+
+/* Where a row of the attended pool comes from. */
+typedef struct qq_token_table {
+  const int32_t* req_to_token; /* device [max_reqs][stride] */
+  int64_t stride;
+} qq_token_table;
+
+/* The new token's K/V write fused into qq_quest_retrieve_topk.
+ * Destination row of request i: dst_rows[i] (Mode 2, out_cache_loc) or,
+ * when dst_rows is NULL, req * (buf + 1) + min(seq_len - 1, buf)
+ * (Mode 3 newest slot, coordinator.py:178-181). */
+typedef struct qq_new_token {
+  const void* k;          /* device [bs][kv_heads*head_dim], pool dtype */
+  const void* v;
+  int64_t src_stride;     /* elements between requests */
+  void* k_dst;            /* layer base of the destination pool */
+  void* v_dst;
+  int64_t dst_row_stride; /* elements between rows */
+  const int64_t* dst_rows;
+  int64_t device_buffer_size;
+  int64_t dst_num_rows;   /* rows of the destination pool; rows outside are skipped */
+  int32_t dtype;
+} qq_new_token;
+
+/* HiSparse state of HiSparseCoordinator (coordinator.py:74-134). */
+typedef struct qq_hisparse_state {
+  int32_t* buffer_tokens;
+  int32_t* lru_slots;
+  int32_t* req_to_host_pool; /* device [max_reqs][max_context_len], -1 = no backup */
+  unsigned long long* stats; /* device [3]: hits, misses, fast_path_calls */
+  int32_t num_layers;
+  int32_t max_reqs;
+  int32_t max_context_len;
+  int32_t device_buffer_size;
+  int32_t top_k;
+} qq_hisparse_state;
+
+/* ---- introspection ---------------------------------------------------- */
+/* Device address of pinned host memory (cudaHostGetDevicePointer); the
+ * HiSparse host tier is read and written by kernels through it. */
+int qq_host_device_pointer(const void* host_ptr, void** device_ptr);
+const char* qq_version(void);
+const char* qq_status_string(int status);
+/* Workspace bytes for calls with up to max_bs requests. */
+size_t qq_workspace_bytes(int max_bs, int top_k, int q_heads, int head_dim);
+
+/* ---- storage initialisation ------------------------------------------ */
+/* Fill bounds and running bounds with the +-bf16max sentinels and zero the
+ * counters.  Replaces QuestAlgorithm.init_storage fills (quest.py:196-208). */
+int qq_quest_init_storage(const qq_quest_state* st, void* stream);
+
+/* Reset one request slot.  Replaces QuestAlgorithm.invalidate_request
+ * (quest.py:468-479). */
+int qq_quest_invalidate(const qq_quest_state* st, int req_pool_idx, void* stream);
+
+/* ---- [Q2] prefill bounds ---------------------------------------------- */
+/* Page bounds of one request's prefill keys for layers [layer_begin,
+ * layer_end): full pages into page_bounds, a partial tail into the running
+ * bounds, counters written when write_counters != 0.  k_layers is a HOST
+ * array of (layer_end - layer_begin) device pointers.  Replaces
+ * QuestAlgorithm.update_prefill_representations (quest.py:231-280), called
+ * per layer by QuestOnlyBackend._update_quest_for_extend (quest_only.py:101-128)
+ * and HiSparseCoordinator.admit_request (coordinator.py:169-172). */
+int qq_quest_bounds_prefill(const qq_quest_state* st, int layer_begin, int layer_end,
+                            const void* const* k_layers, int kv_dtype, int64_t k_row_stride,
+                            const int32_t* prefill_indices, int prefill_len, int req_pool_idx,
+                            int write_counters, void* stream);
+
+/* ---- [Q3] per-step bounds fold + finalize ----------------------------- */
+#define QQ_STEP_FOLD 1     /* running min/max <- key of the previous token */
+#define QQ_STEP_FINALIZE 2 /* finalize pages whose 64th token arrived, advance counters */
+/* For every request i of the batch whose skip flag is clear: fold the key of
+ * its previous token into the running bounds of layers [layer_begin,
+ * layer_end) and/or finalize.  The previous token's row is rows[i] when rows
+ * is given, else req_to_token[req][max(seq_len-2,0)] when table is given,
+ * else req * (buf + 1) + min(seq_len - 2, buf).  skip_flags (device [max_reqs],
+ * nullable) are read and cleared.  Replaces
+ * QuestOnlyBackend._do_quest_decode_step_update (quest_only.py:84-97),
+ * QuestAlgorithm.update_decode_representations and
+ * maybe_finalize_decode_representations (quest.py:284-321) and the bounds
+ * part of HiSparseCoordinator.prepare_decode_step (coordinator.py:199-209). */
+int qq_quest_decode_step(const qq_quest_state* st, int flags, int layer_begin, int layer_end,
+                         const void* const* k_layers, int kv_dtype, int64_t k_row_stride,
+                         const qq_batch* batch, uint8_t* skip_flags, const int64_t* rows,
+                         const qq_token_table* table, int64_t device_buffer_size,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- [Q5] GQA grouping + page scores ---------------------------------- */
+/* out[b][h][d] = mean over the group of q[b][h*G + g][d], in the query dtype.
+ * Replaces QuestAlgorithm.group_queries (quest.py:366-391). */
+int qq_quest_group_queries(const void* q, int dtype, int bs, int q_heads, int kv_heads,
+                           int head_dim, int64_t q_stride, void* out, void* stream);
+
+/* scores[b][p] = sum_{h,d} qg * (qg >= 0 ? kmax : kmin) in fp32 for pages
+ * [0, num_pages) of layer `layer`, with qg the already grouped query
+ * [bs][kv_heads][head_dim].  Replaces QuestAlgorithm.page_scores (quest.py:393-405). */
+int qq_quest_page_scores(const qq_quest_state* st, int layer, const qq_batch* batch,
+                         const void* grouped_q, int q_dtype, int64_t q_stride, int num_pages,
+                         float* scores, void* stream);
+
+/* ---- [Q5][Q6][Q7] fused score + top-k + layout + translation ---------- */
+/* One launch per layer: GQA-mean of q, page scores of the candidate pages,
+ * the top (top_k/page - 1) pages (descending score, ties -> lower page),
+ * their positions followed by the recent window, or the dense layout when
+ * seq_len <= top_k; optional req_to_token translation into rows and the
+ * optional new-token K/V write.  scores (device [bs][max_pages]) receives
+ * the fp32 scores of pages [0, seq_len/page) with -inf for pages that are
+ * not candidates.  Replaces QuestAlgorithm.prepare_step + retrieve_topk
+ * (quest.py:325-464), the req_to_token gather of QuestOnlyBackend.forward_decode
+ * (quest_only.py:153-158) and set_kv_buffer / write_new_token
+ * (memory.py:114-120, coordinator.py:217-228). */
+int qq_quest_retrieve_topk(const qq_quest_state* st, int layer, const qq_batch* batch,
+                           const void* q, int q_dtype, int q_heads, int64_t q_stride,
+                           int32_t* positions, int32_t* actual_lens, float* scores,
+                           const qq_token_table* translate, int32_t* rows,
+                           const qq_new_token* new_token, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* ---- [Q7] sparse decode attention ------------------------------------ */
+/* out[b] = attention of q[b] ([q_heads][head_dim]) over the rows
+ * rows[b][0 .. min(seq_len, top_k)) of k_pool / v_pool (duplicates counted),
+ * fp32 softmax and accumulation, result in the query dtype.  Split over
+ * 128-row chunks, merged in-kernel.  Replaces decode_attention
+ * (attention/ops.py:48-66) as called by QuestOnlyBackend.forward_decode
+ * (quest_only.py:153-158) and QuestHiSparseBackend.forward_decode
+ * (quest_hisparse.py:128-132). */
+int qq_sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, int dtype,
+                               int q_heads, int kv_heads, int head_dim, int64_t q_stride,
+                               const int32_t* rows, const void* k_pool, const void* v_pool,
+                               int64_t kv_row_stride, int64_t num_rows, float scaling,
+                               void* out, int64_t out_stride, uint32_t* err, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* ---- [H3] HiSparse swap-in -------------------------------------------- */
+/* For every request of the batch: fast path (seq_len <= buf: row = slot =
+ * position) or first-occurrence dedupe, hit detection in LRU order,
+ * eviction of the least recently used slots, copy of the misses from the
+ * host tier (mapped pinned memory, read by the kernel), LRU rewrite
+ * [stale evictables | loaded misses | hits] and rows_out[b][j] =
+ * req * (buf + 1) + slot of positions[b][j].  Replaces
+ * HiSparseCoordinator.swap_in_selected_pages / _swap_in_long
+ * (coordinator.py:232-304). */
+int qq_hisparse_swap_in(const qq_hisparse_state* hs, int layer, const qq_batch* batch,
+                        const int32_t* positions, int32_t* rows_out, const void* host_k,
+                        const void* host_v, void* dev_k, void* dev_v, int64_t row_bytes,
+                        uint32_t* err, void* stream);
+
+/* Reset one request slot: buffer_tokens = -1, lru_slots = 0..buf-1,
+ * req_to_host_pool = -1.  Replaces the device part of
+ * HiSparseCoordinator.request_finished (coordinator.py:312-314). */
+int qq_hisparse_reset(const qq_hisparse_state* hs, int req_pool_idx, void* stream);
+
+/* Admission layout: buffer_tokens[:, req, :] = lru_slots[:, req, :] = 0..buf-1
+ * (coordinator.py:166-167). */
+int qq_hisparse_admit_layout(const qq_hisparse_state* hs, int req_pool_idx, void* stream);
+
+/* ---- row copies (admission, eager backup) ----------------------------- */
+/* For every (layer, i < n): dst_layers[layer][dst_idx[i]] <- src_layers[layer][src_idx[i]],
+ * row_bytes bytes per row; strides in bytes; index arrays int32 or int64
+ * (idx_is64 != 0).  src/dst may be device memory or mapped pinned host
+ * memory.  Used for HiSparse admission (coordinator.py:154-164) and the
+ * eager host backup of the previous token (coordinator.py:211-215). */
+int qq_copy_rows(const void* const* src_layers, void* const* dst_layers, int num_layers,
+                 int64_t src_row_stride, int64_t dst_row_stride, int64_t row_bytes,
+                 const void* src_idx, int src_idx_is64, const void* dst_idx, int dst_idx_is64,
+                 int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QQUEST_H */

@@ -1,0 +1,39 @@
+"""qwenquest_b200 — B200-native (sm_100a) Quest sparse-decode path for QwenQuest.
+
+Drop-in attention backends for the reference's ``Engine``:
+
+* :class:`~qwenquest_b200.backends.B200QuestOnlyBackend` (``attention_mode="quest"``)
+* :class:`~qwenquest_b200.backends.B200QuestHiSparseBackend` (``attention_mode="quest_hisparse"``)
+
+plus :class:`~qwenquest_b200.quest.QuestAlgorithm` and
+:class:`~qwenquest_b200.hisparse.HiSparseCoordinator` with the reference's
+APIs.  All decode work runs in hand-written CUDA kernels in ``libqquest.so``
+(C ABI: ``include/qquest.h``); nothing falls back to the CPU.  Importing this
+package does not load the library; the first backend / algorithm object does.
+"""
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "B200QuestHiSparseBackend",
+    "B200QuestOnlyBackend",
+    "HiSparseCoordinator",
+    "QuestAlgorithm",
+    "QuestTrace",
+]
+
+
+def __getattr__(name):
+    if name in ("B200QuestHiSparseBackend", "B200QuestOnlyBackend"):
+        from qwenquest_b200 import backends
+
+        return getattr(backends, name)
+    if name == "HiSparseCoordinator":
+        from qwenquest_b200.hisparse import HiSparseCoordinator
+
+        return HiSparseCoordinator
+    if name in ("QuestAlgorithm", "QuestTrace"):
+        from qwenquest_b200 import quest
+
+        return getattr(quest, name)
+    raise AttributeError(name)

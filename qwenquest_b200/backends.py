@@ -1,0 +1,369 @@
+"""The Quest attention backends on B200 — drop-ins for the reference's
+``QuestOnlyBackend`` (``src/qwenquest/attention/quest_only.py``) and
+``QuestHiSparseBackend`` (``src/qwenquest/attention/quest_hisparse.py``).
+
+Same constructor arguments, class flags, lifecycle hooks and public
+attributes (``.quest``, ``.coord``, ``.sparse_config``); ``Engine.generate``
+runs unchanged once the engine holds one of these as ``attn_backend``.
+
+Per decode step and layer the work is a fixed, small number of launches on
+the current stream with no host synchronisation:
+
+* ``init_forward_metadata``: one ``qq_quest_decode_step`` launch folds the
+  previous token's key into the running bounds of **all** layers and
+  finalizes completed pages (Mode 3 adds the eager host backup launch);
+* ``forward_decode``: one ``qq_quest_retrieve_topk`` launch (new K/V write +
+  GQA mean + page scores + top-k + layout + ``req_to_token`` translation),
+  Mode 3 one ``qq_hisparse_swap_in`` launch, and one
+  ``qq_sparse_decode_attention`` launch.
+
+Prefill stays dense, as in the reference (``attention/base.py:65-93``).
+"""
+
+from __future__ import annotations
+
+from abc import ABC, abstractmethod
+
+import torch
+import torch.nn.functional as F
+
+from qwenquest_b200 import _lib
+from qwenquest_b200._lib import QQ_STEP_FINALIZE, QQ_STEP_FOLD, check
+from qwenquest_b200.config import avoid_recent_overlap, parse_hisparse_config
+from qwenquest_b200.hisparse import HiSparseCoordinator, _DeviceError
+from qwenquest_b200.quest import QuestAlgorithm, dtype_code, stream_of
+
+__all__ = ["AttentionBackend", "B200QuestHiSparseBackend", "B200QuestOnlyBackend", "extend_attention"]
+
+
+def extend_attention(q, k, v, prefix_len: int, scaling: float) -> torch.Tensor:
+    """Dense causal attention of one request's new tokens (semantics of ``attention/ops.py:18-45``)."""
+    n, num_heads, head_dim = q.shape
+    kv_len, kv_heads, _ = k.shape
+    group = num_heads // kv_heads
+    qh = q.transpose(0, 1).unsqueeze(0)
+    kh = k.repeat_interleave(group, dim=1).transpose(0, 1).unsqueeze(0)
+    vh = v.repeat_interleave(group, dim=1).transpose(0, 1).unsqueeze(0)
+    if prefix_len == 0 and n == kv_len:
+        out = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=scaling)
+    else:
+        q_pos = prefix_len + torch.arange(n, device=q.device)
+        mask = torch.arange(kv_len, device=q.device).unsqueeze(0) <= q_pos.unsqueeze(1)
+        out = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask, scale=scaling)
+    return out[0].transpose(0, 1).reshape(n, num_heads * head_dim)
+
+
+class AttentionBackend(ABC):
+    """The interface of ``attention/base.py:20-112``."""
+
+    name: str = ""
+    uses_token_pool_for_decode: bool = True
+    frees_prefill_kv_after_admission: bool = False
+
+    def __init__(self, req_to_token_pool, token_to_kv_pool):
+        self.req_to_token_pool = req_to_token_pool
+        self.token_to_kv_pool = token_to_kv_pool
+
+    @property
+    def req_to_token(self) -> torch.Tensor:
+        return self.req_to_token_pool.req_to_token
+
+    def init_forward_metadata(self, batch) -> None:  # noqa: B027 - optional hook
+        """Per-forward preparation (once, before layer 0)."""
+
+    def forward(self, q, k, v, layer, batch) -> torch.Tensor:
+        if batch.forward_mode.is_decode():
+            return self.forward_decode(q, k, v, layer, batch)
+        return self.forward_extend(q, k, v, layer, batch)
+
+    def forward_extend(self, q, k, v, layer, batch) -> torch.Tensor:
+        """Dense causal prefill: save the new K/V, then attend per request (base.py:65-93)."""
+        assert batch.out_cache_loc is not None
+        assert batch.extend_prefix_lens is not None
+        self.token_to_kv_pool.set_kv_buffer(layer.layer_id, batch.out_cache_loc, k, v)
+        k_buf, v_buf = self.token_to_kv_pool.get_kv_buffer(layer.layer_id)
+        offsets = batch.extend_token_offsets()
+        outputs = []
+        for i in range(batch.batch_size):
+            req = int(batch.req_pool_indices[i])
+            seq_len = int(batch.seq_lens[i])
+            locs = self.req_to_token[req, :seq_len].long()
+            outputs.append(
+                extend_attention(q[offsets[i] : offsets[i + 1]], k_buf[locs], v_buf[locs],
+                                 prefix_len=int(batch.extend_prefix_lens[i]), scaling=layer.scaling)
+            )
+        return torch.cat(outputs, dim=0)
+
+    @abstractmethod
+    def forward_decode(self, q, k, v, layer, batch) -> torch.Tensor:
+        """``q``: ``[bs, H, D]``; ``k``/``v``: ``[bs, KV, D]`` of the new tokens -> ``[bs, H*D]``."""
+
+    def on_extend_finished(self, batch) -> None:  # noqa: B027 - optional hook
+        """Called by the engine after a whole prefill forward (all layers)."""
+
+    def on_request_finished(self, req_pool_idx: int) -> None:  # noqa: B027 - optional hook
+        """Called by the engine before a request slot is reused."""
+
+
+def _parse_quest_config(sparse_config):
+    cfg = parse_hisparse_config(sparse_config)
+    if getattr(cfg, "algorithm", None) != "quest" or getattr(cfg, "quest_page_size", None) is None:
+        raise ValueError("Quest backends require hisparse_config with algorithm='quest'")
+    return cfg
+
+
+class _QuestDecodeMixin:
+    """Shared decode plumbing: step tensors, persistent buffers, the attention launch."""
+
+    quest: QuestAlgorithm
+    device: torch.device
+
+    def _setup_decode(self, max_reqs: int) -> None:
+        dev = self.device
+        top_k = self.quest.top_k
+        self._positions = torch.empty((max_reqs, top_k), dtype=torch.int32, device=dev)
+        self._rows = torch.empty((max_reqs, top_k), dtype=torch.int32, device=dev)
+        self._actual = torch.empty(max_reqs, dtype=torch.int32, device=dev)
+        self._attn_ws: torch.Tensor | None = None
+        self._attn_err = _DeviceError(torch.zeros(1, dtype=torch.int32).pin_memory())
+        self._step_reqs: torch.Tensor | None = None
+        self._step_seq: torch.Tensor | None = None
+        self._max_reqs = max_reqs
+        self.lib = _lib.load()
+
+    def _begin_step(self, batch) -> None:
+        self._step_reqs = batch.req_pool_indices.to(device=self.device, dtype=torch.int64).contiguous()
+        self._step_seq = batch.seq_lens.to(device=self.device, dtype=torch.int64).contiguous()
+        self.quest.prepare_step(self._step_seq)
+
+    def check_errors(self) -> None:
+        """Raise for device errors reported by earlier launches (no synchronisation)."""
+        _lib.raise_device_error(self._attn_err.take(), "(attention)")
+
+    def synchronize(self) -> None:
+        """Wait for this backend's work and raise any device error it reported."""
+        torch.cuda.current_stream(self.device).synchronize()
+        self.check_errors()
+
+    def _workspace(self, q_heads: int, head_dim: int) -> torch.Tensor:
+        need = int(self.lib.qq_workspace_bytes(self._max_reqs, self.quest.top_k, q_heads, head_dim))
+        if self._attn_ws is None or self._attn_ws.numel() < need:
+            self._attn_ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        return self._attn_ws
+
+    def _attend(self, q3, layer, reqs, seq, rows, k_pool, v_pool) -> torch.Tensor:
+        bs, heads, dim = q3.shape
+        out = torch.empty((bs, heads * dim), dtype=q3.dtype, device=self.device)
+        ws = self._workspace(heads, dim)
+        batch = _lib.QQBatch(reqs.data_ptr(), seq.data_ptr(), bs)
+        rc = self.lib.qq_sparse_decode_attention(
+            batch, self.quest.top_k, q3.data_ptr(), dtype_code(q3.dtype), heads, self.quest.kv_heads, dim,
+            q3.stride(0), rows.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), k_pool.stride(0),
+            k_pool.shape[0], float(layer.scaling), out.data_ptr(), out.stride(0), self._attn_err.ptr(),
+            ws.data_ptr(), ws.numel(), stream_of(self.device),
+        )
+        check(rc, "sparse decode attention")
+        return out
+
+    def _new_token(self, k, v, k_dst, v_dst, dst_rows, buf) -> _lib.QQNewToken:
+        dim = self.quest.kv_heads * self.quest.head_dim
+        return _lib.QQNewToken(
+            k.data_ptr(), v.data_ptr(), dim, k_dst.data_ptr(), v_dst.data_ptr(), k_dst.stride(0),
+            dst_rows.data_ptr() if dst_rows is not None else None, int(buf), int(k_dst.shape[0]),
+            dtype_code(k_dst.dtype),
+        )
+
+    def _q3(self, q, bs) -> torch.Tensor:
+        q3 = q.reshape(bs, -1, self.quest.head_dim)
+        if q3.dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError(f"unsupported query dtype {q3.dtype}")
+        return q3.contiguous()
+
+
+class B200QuestOnlyBackend(_QuestDecodeMixin, AttentionBackend):
+    """Mode 2: Quest top-k with the full KV pool on the device (quest_only.py:39-167)."""
+
+    name = "flashinfer_quest"
+
+    def __init__(self, req_to_token_pool, token_to_kv_pool, sparse_config, *, start_layer: int = 0,
+                 end_layer: int | None = None):
+        AttentionBackend.__init__(self, req_to_token_pool, token_to_kv_pool)
+        cfg = _parse_quest_config(sparse_config)
+        self.sparse_config = cfg
+        self.device = torch.device(token_to_kv_pool.device)
+        if self.device.type != "cuda":
+            raise ValueError("B200QuestOnlyBackend needs the KV pool on a CUDA device")
+        self.quest = QuestAlgorithm(top_k=cfg.top_k, page_size=cfg.quest_page_size, device=self.device,
+                                    avoid_recent_overlap=avoid_recent_overlap(cfg))
+        self.device = self.quest.device
+        self.quest.init_storage(
+            start_layer=start_layer,
+            end_layer=token_to_kv_pool.num_layers if end_layer is None else end_layer,
+            max_reqs=req_to_token_pool.size,
+            max_context_len=req_to_token_pool.max_context_len,
+            kv_heads=token_to_kv_pool.kv_heads,
+            head_dim=token_to_kv_pool.head_dim,
+        )
+        self._skip_first_decode_update = torch.zeros(req_to_token_pool.size, dtype=torch.uint8, device=self.device)
+        q = self.quest
+        self._k_layers = _lib.ptr_array(
+            [token_to_kv_pool.get_key_buffer(layer).data_ptr() for layer in range(q.start_layer, q.end_layer)]
+        )
+        kb0 = token_to_kv_pool.get_key_buffer(q.start_layer)
+        self._kv_dtype, self._k_row_stride = dtype_code(kb0.dtype), kb0.stride(0)
+        self._setup_decode(req_to_token_pool.size)
+
+    # ---------------------------------------------------------------- per step
+
+    def init_forward_metadata(self, batch) -> None:
+        if batch.forward_mode.is_decode():
+            self.check_errors()
+            self._begin_step(batch)
+            # [Q3] fold the previous token (seq_len - 2) into all layers' running bounds (quest_only.py:84-97)
+            self.quest.decode_step(
+                QQ_STEP_FOLD | QQ_STEP_FINALIZE, self._step_reqs, self._step_seq, None,
+                skip_flags=self._skip_first_decode_update, req_to_token=self.req_to_token,
+                k_ptrs=self._k_layers[0], kv_dtype=self._kv_dtype, k_row_stride=self._k_row_stride,
+            )
+
+    # ----------------------------------------------------------------- prefill
+
+    def forward_extend(self, q, k, v, layer, batch) -> torch.Tensor:
+        out = super().forward_extend(q, k, v, layer, batch)
+        if layer.layer_id == self.quest.end_layer - 1:
+            self._update_quest_for_extend(batch)
+        return out
+
+    def _update_quest_for_extend(self, batch) -> None:
+        """[Q2] bounds of positions ``0 .. seq_len-1`` of every layer (quest_only.py:101-128)."""
+        q = self.quest
+        kb = [self.token_to_kv_pool.get_key_buffer(layer) for layer in range(q.start_layer, q.end_layer)]
+        for req_idx, seq_len in zip(batch.req_pool_indices.tolist(), batch.seq_lens.tolist(), strict=True):
+            prefill_indices = self.req_to_token[req_idx, :seq_len]
+            q.update_prefill_representations_all_layers(req_idx, kb, prefill_indices)
+            self._skip_first_decode_update[req_idx] = 1
+
+    # ------------------------------------------------------------------ decode
+
+    def forward_decode(self, q, k, v, layer, batch) -> torch.Tensor:
+        assert batch.out_cache_loc is not None
+        li = layer.layer_id
+        if self._step_reqs is None or self._step_reqs.shape[0] != batch.batch_size:
+            self._begin_step(batch)
+        reqs, seq = self._step_reqs, self._step_seq
+        bs = reqs.shape[0]
+        k_buf, v_buf = self.token_to_kv_pool.get_kv_buffer(li)
+        q3 = self._q3(q, bs)
+        kk = k.to(k_buf.dtype).reshape(bs, -1).contiguous()
+        vv = v.to(v_buf.dtype).reshape(bs, -1).contiguous()
+        dst = batch.out_cache_loc.to(device=self.device, dtype=torch.int64).contiguous()
+        nt = self._new_token(kk, vv, k_buf, v_buf, dst, 0)
+        table = _lib.QQTokenTable(self.req_to_token.data_ptr(), self.req_to_token.stride(0))
+        # [Q6] + [Q7] translation + new K/V write, one launch
+        self.quest.select(q3, li, reqs, seq, self._positions, self._actual, translate=table,
+                          rows=self._rows, new_token=nt)
+        # [Q7] attention over exactly those rows (duplicates kept)
+        return self._attend(q3, layer, reqs, seq, self._rows, k_buf, v_buf)
+
+    # --------------------------------------------------------------- lifecycle
+
+    def on_request_finished(self, req_pool_idx: int) -> None:
+        self.quest.invalidate_request(req_pool_idx)
+        self._skip_first_decode_update[req_pool_idx] = 0
+
+
+class B200QuestHiSparseBackend(_QuestDecodeMixin, AttentionBackend):
+    """Mode 3: Quest top-k + HiSparse host tier / LRU hot buffer (quest_hisparse.py:44-138)."""
+
+    name = "flashinfer_hisparse"
+    uses_token_pool_for_decode = False
+    frees_prefill_kv_after_admission = True
+
+    def __init__(self, req_to_token_pool, token_to_kv_pool, sparse_config, *, host_pool_size: int,
+                 start_layer: int = 0, end_layer: int | None = None, host_device="cpu",
+                 host_layers: int | None = None):
+        AttentionBackend.__init__(self, req_to_token_pool, token_to_kv_pool)
+        cfg = _parse_quest_config(sparse_config)
+        self.sparse_config = cfg
+        self.device = torch.device(token_to_kv_pool.device)
+        if self.device.type != "cuda":
+            raise ValueError("B200QuestHiSparseBackend needs the KV pool on a CUDA device")
+        num_layers = token_to_kv_pool.num_layers
+        self.quest = QuestAlgorithm(top_k=cfg.top_k, page_size=cfg.quest_page_size, device=self.device,
+                                    avoid_recent_overlap=avoid_recent_overlap(cfg))
+        self.device = self.quest.device
+        self.quest.init_storage(
+            start_layer=start_layer,
+            end_layer=num_layers if end_layer is None else end_layer,
+            max_reqs=req_to_token_pool.size,
+            max_context_len=req_to_token_pool.max_context_len,
+            kv_heads=token_to_kv_pool.kv_heads,
+            head_dim=token_to_kv_pool.head_dim,
+        )
+        self.coord = HiSparseCoordinator(
+            quest=self.quest,
+            num_layers=num_layers,
+            kv_heads=token_to_kv_pool.kv_heads,
+            head_dim=token_to_kv_pool.head_dim,
+            max_reqs=req_to_token_pool.size,
+            max_context_len=req_to_token_pool.max_context_len,
+            top_k=cfg.top_k,
+            device_buffer_size=cfg.device_buffer_size,
+            host_pool_size=host_pool_size,
+            dtype=token_to_kv_pool.dtype,
+            device=self.device,
+            host_device=host_device,
+            host_layers=host_layers,
+        )
+        self._setup_decode(req_to_token_pool.size)
+
+    def check_errors(self) -> None:
+        super().check_errors()
+        self.coord.check_errors("(swap-in)")
+
+    def init_forward_metadata(self, batch) -> None:
+        if batch.forward_mode.is_decode():
+            self.check_errors()
+            self.coord.prepare_decode_step(batch.req_pool_indices, batch.seq_lens)
+            self._begin_step(batch)
+
+    def on_extend_finished(self, batch) -> None:
+        for req_idx, seq_len in zip(batch.req_pool_indices.tolist(), batch.seq_lens.tolist(), strict=True):
+            prefill_indices = self.req_to_token[req_idx, :seq_len]
+            self.coord.admit_request(req_idx, seq_len, self.token_to_kv_pool, prefill_indices)
+
+    def forward_decode(self, q, k, v, layer, batch) -> torch.Tensor:
+        li = layer.layer_id
+        if self._step_reqs is None or self._step_reqs.shape[0] != batch.batch_size:
+            self._begin_step(batch)
+        reqs, seq = self._step_reqs, self._step_seq
+        bs = reqs.shape[0]
+        coord = self.coord
+        k_dev, v_dev = coord.device_k[li], coord.device_v[li]
+        q3 = self._q3(q, bs)
+        kk = k.to(k_dev.dtype).reshape(bs, -1).contiguous()
+        vv = v.to(v_dev.dtype).reshape(bs, -1).contiguous()
+        # 1. new K/V into the newest slot, 2. [Q6] selection — one launch
+        nt = self._new_token(kk, vv, k_dev, v_dev, None, coord.device_buffer_size)
+        self.quest.select(q3, li, reqs, seq, self._positions, self._actual, new_token=nt)
+        # 3. [H3] positions -> hot-buffer rows (misses copied from the host tier)
+        coord.swap_in(reqs, seq, self._positions, li, self._rows)
+        # 4. [Q7] attention over the hot buffer
+        return self._attend(q3, layer, reqs, seq, self._rows, k_dev, v_dev)
+
+    def on_request_finished(self, req_pool_idx: int) -> None:
+        self.check_errors()
+        self.coord.request_finished(req_pool_idx)
+
+
+def _register_with_reference() -> None:
+    """Make ``isinstance(b, qwenquest...AttentionBackend)`` true when the reference is installed."""
+    try:
+        from qwenquest.attention.base import AttentionBackend as RefBackend  # type: ignore
+    except Exception:
+        return
+    for cls in (B200QuestOnlyBackend, B200QuestHiSparseBackend):
+        RefBackend.register(cls)
+
+
+_register_with_reference()

@@ -1,0 +1,542 @@
+// [Q7] Split-K sparse decode attention over an explicit row list.
+//
+// Fast path (bf16, 4 KV heads, head_dim 128, 8 query heads per KV head):
+// a persistent kernel, one block per SM.  Work items are (request, chunk of
+// 128 rows).  Warp 8 is the producer: for each stage of 32 rows its lanes
+// issue one 1 KiB cp.async.bulk for the K row and one for the V row (the
+// whole row: all 4 KV heads), completing on the stage's mbarrier; rows land
+// at a 1040-byte pitch so ldmatrix reads are bank-conflict free.  Warps 0-7
+// are consumers, warp w owning KV head w%4 and half w/4 of every stage:
+//   S^T[16 rows x 8 heads] = K[16 x 128] . Q^T[128 x 8]   (8 x mma m16n8k16)
+//   online softmax in fp32 (exp2 domain), P^T via movmatrix.trans
+//   O^T[128 x 8] += V^T[128 x 16] . P^T[16 x 8]          (8 x mma m16n8k16)
+// The two halves of a head merge through shared memory at the end of the
+// item; chunks of one request merge in the last block to finish (arrival
+// counter in the workspace).  Per row the kernel reads 2 KiB and does 16 K
+// FMA-equivalents on the tensor cores, so it is HBM-bound.
+//
+// Generic path (any head_dim / group / fp32): one block per (request, KV
+// head), scores in shared memory, two-pass softmax, fp32 FMA.
+
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace qq {
+namespace {
+
+// ------------------------------------------------------------------ fast path constants
+constexpr int kD = 128;
+constexpr int kKV = 4;
+constexpr int kG = 8;
+constexpr int kH = kKV * kG;
+constexpr int kRowBytes = kKV * kD * 2;    // 1024
+constexpr int kPitch = kRowBytes + 16;     // 1040
+constexpr int kToks = 32;                  // rows per stage
+constexpr int kStages = 3;
+constexpr int kChunk = kAttnChunk;         // 128 rows per work item
+constexpr int kConsumerWarps = 8;
+constexpr int kThreadsFast = (kConsumerWarps + 1) * 32;
+constexpr int kStageBytes = 2 * kToks * kPitch;  // K tile + V tile
+constexpr int kMergeFloats = kKV * kG * kD;     // 4096
+constexpr size_t kSmemFast =
+    (size_t)kStages * kStageBytes + sizeof(float) * (kMergeFloats + 2 * kKV * kG) + 2 * kStages * 8 + 16;
+
+struct AttnArgs {
+  const int64_t* seq_lens;
+  int bs;
+  int top_k;
+  int max_chunks;
+  const void* q;
+  int64_t q_stride;
+  const int32_t* rows;
+  const char* k_pool;
+  const char* v_pool;
+  int64_t row_stride_bytes;
+  int64_t num_rows;
+  float scale_log2;  // scaling * log2(e)
+  float scaling;
+  void* out;
+  int64_t out_stride;
+  uint32_t* err;
+  float* part_o;   // [bs * max_chunks][kH][kD]
+  float* part_ml;  // [bs * max_chunks][kH][2]
+  int32_t* counters;
+};
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                            uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                                  uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const uint32_t l = f32_to_bf16_bits(lo), h = f32_to_bf16_bits(hi);
+  return (h << 16) | l;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
+
+#define kNegInf (-__int_as_float(0x7f800000))
+
+__device__ __forceinline__ int item_rows(const AttnArgs& a, int item, int& req, int& base) {
+  req = item / a.max_chunks;
+  const int c = item - req * a.max_chunks;
+  const int64_t L = a.seq_lens[req];
+  const int n = (int)(L < a.top_k ? L : a.top_k);
+  base = c * kChunk;
+  const int cnt = n - base;
+  return cnt <= 0 ? 0 : (cnt < kChunk ? cnt : kChunk);
+}
+
+__global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) {
+  extern __shared__ __align__(128) char smem[];
+  char* s_stage = smem;
+  float* s_merge = reinterpret_cast<float*>(smem + (size_t)kStages * kStageBytes);
+  float* s_mm = s_merge + kMergeFloats;  // [kKV][kG] m
+  float* s_ml = s_mm + kKV * kG;         // [kKV][kG] l
+  uint64_t* s_full = reinterpret_cast<uint64_t*>(s_ml + kKV * kG);
+  uint64_t* s_empty = s_full + kStages;
+  int* s_flag = reinterpret_cast<int*>(s_empty + kStages);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int total_items = a.bs * a.max_chunks;
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t ephase = 1;  // a fresh barrier's preceding phase counts as complete
+    for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
+      int req, base;
+      const int cnt = item_rows(a, item, req, base);
+      if (cnt == 0) continue;
+      const int32_t* rows = a.rows + (int64_t)req * a.top_k + base;
+      for (int s0 = 0; s0 < cnt; s0 += kToks) {
+        if (!mbar_wait(&s_empty[stage], ephase)) {
+          raise_error(a.err, QQ_DEV_ERR_TIMEOUT);
+          return;
+        }
+        const int ntok = min(kToks, cnt - s0);
+        char* sk = s_stage + (size_t)stage * kStageBytes;
+        char* sv = sk + kToks * kPitch;
+        if (ntok < kToks) {
+          if (lane >= ntok) {  // rows past the end: zero V so that 0 * V stays 0
+            uint4* z = reinterpret_cast<uint4*>(sv + lane * kPitch);
+            for (int w = 0; w < kRowBytes / 16; ++w) z[w] = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&s_full[stage], (uint32_t)ntok * 2u * kRowBytes);
+        __syncwarp();
+        if (lane < ntok) {
+          int64_t row = rows[s0 + lane];
+          if (row < 0 || row >= a.num_rows) {
+            raise_error(a.err, QQ_DEV_ERR_BOUNDS);
+            row = 0;
+          }
+          bulk_g2s(sk + lane * kPitch, a.k_pool + row * a.row_stride_bytes, kRowBytes, &s_full[stage]);
+          bulk_g2s(sv + lane * kPitch, a.v_pool + row * a.row_stride_bytes, kRowBytes, &s_full[stage]);
+        }
+        if (++stage == kStages) {
+          stage = 0;
+          ephase ^= 1;
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int h = warp & 3;      // KV head
+  const int half = warp >> 2;  // which 16 rows of each stage
+  const int gid = lane >> 2, tig = lane & 3;
+  int stage = 0;
+  uint32_t fphase = 0;
+  const __nv_bfloat16* qbase = static_cast<const __nv_bfloat16*>(a.q);
+
+  for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
+    int req, base;
+    const int cnt = item_rows(a, item, req, base);
+    if (cnt == 0) continue;
+    const int chunk = base / kChunk;
+    const int nchunks = (int)(((a.seq_lens[req] < a.top_k ? a.seq_lens[req] : a.top_k) + kChunk - 1) / kChunk);
+
+    // Q^T fragments of KV head h: B[k = d][n = query head g]
+    uint32_t qb[8][2];
+    {
+      const uint32_t* qrow =
+          reinterpret_cast<const uint32_t*>(qbase + (int64_t)req * a.q_stride + (int64_t)(h * kG + gid) * kD);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        qb[kk][0] = __ldg(qrow + (kk * 16 + 2 * tig) / 2);
+        qb[kk][1] = __ldg(qrow + (kk * 16 + 8 + 2 * tig) / 2);
+      }
+    }
+    float acc[8][4];
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+    float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
+
+    for (int s0 = 0; s0 < cnt; s0 += kToks) {
+      if (!mbar_wait(&s_full[stage], fphase)) {
+        raise_error(a.err, QQ_DEV_ERR_TIMEOUT);
+        return;
+      }
+      const int ntok = min(kToks, cnt - s0);
+      const char* sk = s_stage + (size_t)stage * kStageBytes;
+      const char* sv = sk + kToks * kPitch;
+      const int t0 = half * 16 + gid, t1 = t0 + 8;
+      if (half * 16 < ntok) {
+        // ---- S^T = K . Q^T
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t kaddr = smem_u32(sk + (half * 16 + (lane & 15)) * kPitch + h * (kD * 2) + (lane >> 4) * 16);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4(a0, a1, a2, a3, kaddr + kk * 32);
+          mma_bf16_16816(c, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+        }
+        // ---- online softmax (exp2 domain); rows >= ntok are masked
+        const bool v0 = t0 < ntok, v1 = t1 < ntok;
+        const float s00 = v0 ? c[0] * a.scale_log2 : kNegInf;  // row t0, head 2tig
+        const float s01 = v0 ? c[1] * a.scale_log2 : kNegInf;  // row t0, head 2tig+1
+        const float s10 = v1 ? c[2] * a.scale_log2 : kNegInf;  // row t1, head 2tig
+        const float s11 = v1 ? c[3] * a.scale_log2 : kNegInf;  // row t1, head 2tig+1
+        float mx_a = fmaxf(s00, s10), mx_b = fmaxf(s01, s11);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o));
+          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
+        }
+        const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+        const float al_a = mn_a == kNegInf ? 1.f : fast_exp2(m_a - mn_a);
+        const float al_b = mn_b == kNegInf ? 1.f : fast_exp2(m_b - mn_b);
+        const float p00 = mn_a == kNegInf ? 0.f : fast_exp2(s00 - mn_a);
+        const float p10 = mn_a == kNegInf ? 0.f : fast_exp2(s10 - mn_a);
+        const float p01 = mn_b == kNegInf ? 0.f : fast_exp2(s01 - mn_b);
+        const float p11 = mn_b == kNegInf ? 0.f : fast_exp2(s11 - mn_b);
+        m_a = mn_a;
+        m_b = mn_b;
+        l_a = l_a * al_a + p00 + p10;
+        l_b = l_b * al_b + p01 + p11;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          acc[mt][0] *= al_a;
+          acc[mt][1] *= al_b;
+          acc[mt][2] *= al_a;
+          acc[mt][3] *= al_b;
+        }
+        // ---- P^T fragments (rows x heads -> heads x rows) and O^T += V^T . P^T
+        const uint32_t pb0 = movmatrix_trans(pack_bf16x2(p00, p01));
+        const uint32_t pb1 = movmatrix_trans(pack_bf16x2(p10, p11));
+        const int j = lane >> 3, r = lane & 7;
+        const uint32_t vaddr =
+            smem_u32(sv + (half * 16 + (j >> 1) * 8 + r) * kPitch + h * (kD * 2) + (j & 1) * 16);
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(a0, a1, a2, a3, vaddr + mt * 32);
+          mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[stage]);
+      if (++stage == kStages) {
+        stage = 0;
+        fphase ^= 1;
+      }
+    }
+
+    // ---- per-thread l partials -> per-head sums
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      l_a += __shfl_xor_sync(0xffffffffu, l_a, o);
+      l_b += __shfl_xor_sync(0xffffffffu, l_b, o);
+    }
+    // ---- merge the two halves of head h through shared memory
+    float* mo = s_merge + h * (kG * kD);
+    if (half == 1) {
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int d0 = mt * 16 + gid;
+        mo[(2 * tig) * kD + d0] = acc[mt][0];
+        mo[(2 * tig + 1) * kD + d0] = acc[mt][1];
+        mo[(2 * tig) * kD + d0 + 8] = acc[mt][2];
+        mo[(2 * tig + 1) * kD + d0 + 8] = acc[mt][3];
+      }
+      if (gid == 0) {
+        s_mm[h * kG + 2 * tig] = m_a;
+        s_mm[h * kG + 2 * tig + 1] = m_b;
+        s_ml[h * kG + 2 * tig] = l_a;
+        s_ml[h * kG + 2 * tig + 1] = l_b;
+      }
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (half == 0) {
+      const float mo_a = s_mm[h * kG + 2 * tig], mo_b = s_mm[h * kG + 2 * tig + 1];
+      const float lo_a = s_ml[h * kG + 2 * tig], lo_b = s_ml[h * kG + 2 * tig + 1];
+      const float M_a = fmaxf(m_a, mo_a), M_b = fmaxf(m_b, mo_b);
+      const float fa_a = m_a == kNegInf ? 0.f : fast_exp2(m_a - M_a);
+      const float fo_a = mo_a == kNegInf ? 0.f : fast_exp2(mo_a - M_a);
+      const float fa_b = m_b == kNegInf ? 0.f : fast_exp2(m_b - M_b);
+      const float fo_b = mo_b == kNegInf ? 0.f : fast_exp2(mo_b - M_b);
+      const float L_a = l_a * fa_a + lo_a * fo_a, L_b = l_b * fa_b + lo_b * fo_b;
+      const int qh_a = h * kG + 2 * tig, qh_b = qh_a + 1;  // query heads of this thread
+      if (nchunks == 1) {
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)req * a.out_stride;
+        const float inv_a = 1.f / L_a, inv_b = 1.f / L_b;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int d0 = mt * 16 + gid;
+          out[qh_a * kD + d0] =
+              __float2bfloat16_rn((acc[mt][0] * fa_a + mo[(2 * tig) * kD + d0] * fo_a) * inv_a);
+          out[qh_b * kD + d0] =
+              __float2bfloat16_rn((acc[mt][1] * fa_b + mo[(2 * tig + 1) * kD + d0] * fo_b) * inv_b);
+          out[qh_a * kD + d0 + 8] =
+              __float2bfloat16_rn((acc[mt][2] * fa_a + mo[(2 * tig) * kD + d0 + 8] * fo_a) * inv_a);
+          out[qh_b * kD + d0 + 8] =
+              __float2bfloat16_rn((acc[mt][3] * fa_b + mo[(2 * tig + 1) * kD + d0 + 8] * fo_b) * inv_b);
+        }
+      } else {
+        const int64_t pidx = (int64_t)req * a.max_chunks + chunk;
+        float* po = a.part_o + pidx * (kH * kD);
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int d0 = mt * 16 + gid;
+          po[qh_a * kD + d0] = acc[mt][0] * fa_a + mo[(2 * tig) * kD + d0] * fo_a;
+          po[qh_b * kD + d0] = acc[mt][1] * fa_b + mo[(2 * tig + 1) * kD + d0] * fo_b;
+          po[qh_a * kD + d0 + 8] = acc[mt][2] * fa_a + mo[(2 * tig) * kD + d0 + 8] * fo_a;
+          po[qh_b * kD + d0 + 8] = acc[mt][3] * fa_b + mo[(2 * tig + 1) * kD + d0 + 8] * fo_b;
+        }
+        if (gid == 0) {
+          float* pml = a.part_ml + pidx * (kH * 2);
+          pml[qh_a * 2] = M_a;
+          pml[qh_a * 2 + 1] = L_a;
+          pml[qh_b * 2] = M_b;
+          pml[qh_b * 2 + 1] = L_b;
+        }
+        __threadfence();
+      }
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (nchunks > 1) {
+      // ---- the last chunk of the request to finish merges all chunks
+      if (tid == 0) {
+        const int old = atomicAdd(&a.counters[req], 1);
+        *s_flag = old == nchunks - 1;
+      }
+      named_bar_sync(1, kConsumerWarps * 32);
+      if (*s_flag) {
+        __threadfence();
+        const float* pml = a.part_ml + (int64_t)req * a.max_chunks * (kH * 2);
+        const float* po = a.part_o + (int64_t)req * a.max_chunks * (kH * kD);
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)req * a.out_stride;
+        for (int e = tid; e < kH * kD; e += kConsumerWarps * 32) {
+          const int qh = e / kD;
+          float M = kNegInf;
+          for (int c = 0; c < nchunks; ++c) M = fmaxf(M, __ldcg(pml + c * (kH * 2) + qh * 2));
+          float S = 0.f, O = 0.f;
+          for (int c = 0; c < nchunks; ++c) {
+            const float f = fast_exp2(__ldcg(pml + c * (kH * 2) + qh * 2) - M);
+            S += __ldcg(pml + c * (kH * 2) + qh * 2 + 1) * f;
+            O += __ldcg(po + c * (kH * kD) + e) * f;
+          }
+          out[e] = __float2bfloat16_rn(O / S);
+        }
+        if (tid == 0) a.counters[req] = 0;
+      }
+      named_bar_sync(1, kConsumerWarps * 32);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ generic path
+
+template <typename T>
+__global__ void attn_generic_kernel(AttnArgs a, int q_heads, int kv_heads, int D) {
+  extern __shared__ float gsm[];
+  const int i = blockIdx.x, h = blockIdx.y;
+  const int G = q_heads / kv_heads;
+  const int64_t L = a.seq_lens[i];
+  const int n = (int)(L < a.top_k ? L : a.top_k);
+  float* q_s = gsm;                 // [G][D]
+  float* s_s = gsm + G * D;         // [G][top_k]
+  float* red = s_s + G * a.top_k;   // [G][2]
+  const T* q = static_cast<const T*>(a.q) + (int64_t)i * a.q_stride + (int64_t)h * G * D;
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) q_s[e] = Elem<T>::load(q + e);
+  __syncthreads();
+  const int32_t* rows = a.rows + (int64_t)i * a.top_k;
+  const int64_t rs = a.row_stride_bytes / (int64_t)sizeof(T);
+  const T* K = reinterpret_cast<const T*>(a.k_pool);
+  const T* V = reinterpret_cast<const T*>(a.v_pool);
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    int64_t row = rows[t];
+    if (row < 0 || row >= a.num_rows) {
+      raise_error(a.err, QQ_DEV_ERR_BOUNDS);
+      row = 0;
+    }
+    const T* kr = K + row * rs + (int64_t)h * D;
+    for (int g = 0; g < G; ++g) {
+      float dot = 0.f;
+      for (int d = 0; d < D; ++d) dot = fmaf(q_s[g * D + d], Elem<T>::load(kr + d), dot);
+      s_s[g * a.top_k + t] = dot * a.scaling;
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int g = warp; g < G; g += nw) {
+    float m = -FLT_MAX;
+    for (int t = lane; t < n; t += 32) m = fmaxf(m, s_s[g * a.top_k + t]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.f;
+    for (int t = lane; t < n; t += 32) {
+      const float p = expf(s_s[g * a.top_k + t] - m);
+      s_s[g * a.top_k + t] = p;
+      sum += p;
+    }
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[g] = sum;
+  }
+  __syncthreads();
+  T* out = static_cast<T*>(a.out) + (int64_t)i * a.out_stride + (int64_t)h * G * D;
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int g = e / D, d = e - g * D;
+    float acc = 0.f;
+    for (int t = 0; t < n; ++t) {
+      int64_t row = rows[t];
+      if (row < 0 || row >= a.num_rows) row = 0;
+      acc = fmaf(s_s[g * a.top_k + t], Elem<T>::load(V + row * rs + (int64_t)h * D + d), acc);
+    }
+    Elem<T>::store(out + e, acc / red[g]);
+  }
+}
+
+int g_sm_count = 0;
+
+int sm_count() {
+  if (g_sm_count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (g_sm_count <= 0) g_sm_count = 148;
+  }
+  return g_sm_count;
+}
+
+}  // namespace
+}  // namespace qq
+
+using namespace qq;
+
+extern "C" size_t qq_workspace_bytes(int max_bs, int top_k, int q_heads, int head_dim) {
+  if (max_bs < 0 || top_k < 0 || q_heads < 0 || head_dim < 0) return 0;
+  return kPartialOffset + sizeof(float) * attn_partial_floats(max_bs, top_k, q_heads, head_dim) + 256;
+}
+
+extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, int dtype,
+                                          int q_heads, int kv_heads, int head_dim, int64_t q_stride,
+                                          const int32_t* rows, const void* k_pool, const void* v_pool,
+                                          int64_t kv_row_stride, int64_t num_rows, float scaling,
+                                          void* out, int64_t out_stride, uint32_t* err, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  if (batch == nullptr || q == nullptr || rows == nullptr || k_pool == nullptr || v_pool == nullptr ||
+      out == nullptr || top_k <= 0 || kv_heads <= 0 || head_dim <= 0 || q_heads % kv_heads != 0 ||
+      num_rows <= 0)
+    return QQ_ERR_INVALID;
+  if (batch->bs == 0) return QQ_OK;
+  if (batch->bs < 0 || batch->bs > QQ_MAX_BS || batch->seq_lens == nullptr) return QQ_ERR_INVALID;
+  if (dtype != QQ_BF16 && dtype != QQ_F32) return QQ_ERR_INVALID;
+  if (workspace == nullptr || workspace_bytes < qq_workspace_bytes(batch->bs, top_k, q_heads, head_dim))
+    return QQ_ERR_WORKSPACE;
+  const int esz = dtype == QQ_BF16 ? 2 : 4;
+  AttnArgs a{};
+  a.seq_lens = batch->seq_lens;
+  a.bs = batch->bs;
+  a.top_k = top_k;
+  a.max_chunks = (top_k + kAttnChunk - 1) / kAttnChunk;
+  a.q = q;
+  a.q_stride = q_stride;
+  a.rows = rows;
+  a.k_pool = static_cast<const char*>(k_pool);
+  a.v_pool = static_cast<const char*>(v_pool);
+  a.row_stride_bytes = kv_row_stride * esz;
+  a.num_rows = num_rows;
+  a.scaling = scaling;
+  a.scale_log2 = scaling * 1.4426950408889634f;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.err = err;
+  char* ws = static_cast<char*>(workspace);
+  a.part_o = reinterpret_cast<float*>(ws + kPartialOffset);
+  a.part_ml = a.part_o + (size_t)batch->bs * a.max_chunks * q_heads * head_dim;
+  a.counters = ws_counters(workspace, kCounterAttn);
+  cudaStream_t s = as_stream(stream);
+
+  const bool fast = dtype == QQ_BF16 && kv_heads == kKV && head_dim == kD && q_heads == kH &&
+                    kv_row_stride == kKV * kD && (reinterpret_cast<uintptr_t>(k_pool) % 16) == 0 &&
+                    (reinterpret_cast<uintptr_t>(v_pool) % 16) == 0 && (q_stride % 2) == 0;
+  if (fast) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      if (cudaFuncSetAttribute(attn_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemFast) !=
+          cudaSuccess)
+        return QQ_ERR_CUDA;
+      attr_set = true;
+    }
+    const int items = batch->bs * a.max_chunks;
+    const int grid = std::min(items, sm_count());
+    attn_fast_kernel<<<grid, kThreadsFast, kSmemFast, s>>>(a);
+    return launch_status();
+  }
+  const int G = q_heads / kv_heads;
+  const size_t smem = sizeof(float) * ((size_t)G * head_dim + (size_t)G * top_k + 2 * (size_t)G);
+  if (smem > 200 * 1024) return QQ_ERR_UNSUPPORTED;
+  dim3 grid(batch->bs, kv_heads);
+  if (dtype == QQ_BF16) {
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(attn_generic_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return QQ_ERR_CUDA;
+    attn_generic_kernel<__nv_bfloat16><<<grid, 128, smem, s>>>(a, q_heads, kv_heads, head_dim);
+  } else {
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(attn_generic_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+      return QQ_ERR_CUDA;
+    attn_generic_kernel<float><<<grid, 128, smem, s>>>(a, q_heads, kv_heads, head_dim);
+  }
+  return launch_status();
+}

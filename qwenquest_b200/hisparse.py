@@ -1,0 +1,294 @@
+"""``HiSparseCoordinator`` on B200: the API of ``src/qwenquest/hisparse/coordinator.py:74-324``.
+
+Two tiers, as in the reference:
+
+* host: every request's full KV history in **pinned** host memory
+  (``host_k/v[layer]``, ``[host_pool_size + 1, kv_heads, head_dim]``), mapped
+  into the device address space so kernels read misses and write backups
+  directly (zero-copy over the host link, no staging copies);
+* device: per request a hot buffer of ``device_buffer_size`` LRU slots plus
+  the reserved newest-token slot (``device_k/v[layer]``), with
+  ``buffer_tokens`` / ``lru_slots`` (int32) describing it.
+
+The swap-in (dedupe, hit detection, eviction, host->device copy, LRU
+rewrite, row lookup) is one kernel launch per layer (``qq_hisparse_swap_in``);
+the eager host backup of the previous token and admission copies are
+``qq_copy_rows`` launches.  The host-row free list stays on the host, as in
+the reference, so ``prepare_decode_step`` reads the batch's request ids and
+lengths on the host once per step.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from qwenquest_b200 import _lib
+from qwenquest_b200._lib import QQ_STEP_FINALIZE, QQ_STEP_FOLD, check
+from qwenquest_b200.memory import TokenToKVPoolAllocator
+from qwenquest_b200.quest import QuestAlgorithm, dtype_code, stream_of
+
+__all__ = ["HiSparseCoordinator", "SwapInStats"]
+
+
+class SwapInStats:
+    """``SwapInStats`` (coordinator.py:48-59), counted on the device; reading syncs."""
+
+    def __init__(self, counters: torch.Tensor):
+        self._c = counters  # int64 [3]: hits, misses, fast_path_calls
+
+    @property
+    def hits(self) -> int:
+        return int(self._c[0])
+
+    @property
+    def misses(self) -> int:
+        return int(self._c[1])
+
+    @property
+    def fast_path_calls(self) -> int:
+        return int(self._c[2])
+
+    @property
+    def hit_rate(self) -> float:
+        total = self.hits + self.misses
+        return self.hits / total if total else float("nan")
+
+    def __repr__(self) -> str:
+        return f"SwapInStats(hits={self.hits}, misses={self.misses}, fast_path_calls={self.fast_path_calls})"
+
+
+def host_device_pointer(t: torch.Tensor) -> int:
+    """Device address of a pinned host tensor (``cudaHostGetDevicePointer``)."""
+    if not t.is_pinned():
+        raise ValueError("the host tier must be pinned memory")
+    out = ctypes.c_void_p()
+    check(_lib.load().qq_host_device_pointer(t.data_ptr(), ctypes.byref(out)), "host_device_pointer")
+    return int(out.value)
+
+
+@dataclass
+class _DeviceError:
+    word: torch.Tensor  # pinned host int32 [1]; kernels OR error bits into it
+    dev_ptr: int = 0
+
+    def ptr(self) -> int:
+        if not self.dev_ptr:
+            self.dev_ptr = host_device_pointer(self.word)
+        return self.dev_ptr
+
+    def take(self) -> int:
+        bits = int(self.word[0])
+        if bits:
+            self.word.zero_()
+        return bits
+
+
+class HiSparseCoordinator:
+    def __init__(
+        self,
+        *,
+        quest: QuestAlgorithm,
+        num_layers: int,
+        kv_heads: int,
+        head_dim: int,
+        max_reqs: int,
+        max_context_len: int,
+        top_k: int,
+        device_buffer_size: int,
+        host_pool_size: int,
+        dtype: torch.dtype,
+        device,
+        host_device="cpu",
+        host_layers: int | None = None,
+    ):
+        # coordinator.py:91-94
+        if device_buffer_size < top_k:
+            raise ValueError("device_buffer_size must be >= top_k")
+        if quest.top_k != top_k:
+            raise ValueError(f"QuestAlgorithm.top_k ({quest.top_k}) != top_k ({top_k})")
+        if torch.device(host_device).type != "cpu":
+            raise ValueError("the HiSparse host tier lives in pinned CPU memory")
+        if not 0 < num_layers <= _lib.QQ_MAX_LAYERS:
+            raise ValueError(f"num_layers must be in [1, {_lib.QQ_MAX_LAYERS}]")
+        self.lib = _lib.load()
+        self.quest = quest
+        self.num_layers = num_layers
+        self.top_k = top_k
+        self.device_buffer_size = buf = device_buffer_size
+        self.device = quest.device
+        self.host_device = torch.device("cpu")
+        self.kv_heads, self.head_dim, self.dtype = kv_heads, head_dim, dtype
+        self.max_reqs, self.max_context_len = max_reqs, max_context_len
+        dev = self.device
+
+        # ---- host tier (pinned, device-mapped)
+        self.host_allocator = TokenToKVPoolAllocator(host_pool_size, device="cpu")
+        hshape = (host_pool_size + 1, kv_heads, head_dim)
+        # host_layers < num_layers aliases layer l onto host buffer l % host_layers
+        # (benchmarks whose full host history would not fit in host RAM)
+        nh = num_layers if host_layers is None else host_layers
+        hk = [torch.zeros(hshape, dtype=dtype).pin_memory() for _ in range(nh)]
+        hv = [torch.zeros(hshape, dtype=dtype).pin_memory() for _ in range(nh)]
+        self.host_k = [hk[i % nh] for i in range(num_layers)]
+        self.host_v = [hv[i % nh] for i in range(num_layers)]
+        self.req_to_host_pool = torch.full((max_reqs, max_context_len), -1, dtype=torch.int32, device=dev)
+
+        # ---- device tier
+        dshape = (max_reqs * (buf + 1), kv_heads, head_dim)
+        self.device_k = [torch.zeros(dshape, dtype=dtype, device=dev) for _ in range(num_layers)]
+        self.device_v = [torch.zeros(dshape, dtype=dtype, device=dev) for _ in range(num_layers)]
+        self.req_to_device_buffer = torch.arange(max_reqs * (buf + 1), dtype=torch.int64, device=dev).view(
+            max_reqs, buf + 1
+        )
+        self.buffer_tokens = torch.full((num_layers, max_reqs, buf), -1, dtype=torch.int32, device=dev)
+        self._lru_init = torch.arange(buf, dtype=torch.int32, device=dev)
+        self.lru_slots = self._lru_init.repeat(num_layers, max_reqs, 1).contiguous()
+        self._skip_first_backup = [False] * max_reqs
+        self._stats = torch.zeros(3, dtype=torch.int64, device=dev)
+        self.stats = SwapInStats(self._stats)
+        self._err = _DeviceError(torch.zeros(1, dtype=torch.int32).pin_memory())
+        self._hs = _lib.QQHiSparseState(
+            self.buffer_tokens.data_ptr(), self.lru_slots.data_ptr(), self.req_to_host_pool.data_ptr(),
+            self._stats.data_ptr(), num_layers, max_reqs, max_context_len, buf, top_k,
+        )
+        self.row_bytes = kv_heads * head_dim * torch.empty(0, dtype=dtype).element_size()
+        # per-layer pointer arrays (K layers then V layers)
+        self._dev_ptrs = _lib.ptr_array([t.data_ptr() for t in self.device_k + self.device_v])
+        self._host_ptrs = _lib.ptr_array([host_device_pointer(t) for t in self.host_k + self.host_v])
+        self._dev_k_ptrs = _lib.ptr_array([t.data_ptr() for t in self.device_k[quest.start_layer:quest.end_layer]])
+
+    def _stream(self) -> int:
+        return stream_of(self.device)
+
+    def check_errors(self, what: str = "") -> None:
+        _lib.raise_device_error(self._err.take(), what)
+
+    # -------------------------------------------------- [H1] admission
+
+    def admit_request(self, req_pool_idx, prefill_len, token_to_kv_pool, prefill_indices) -> None:
+        """[H1] (coordinator.py:138-174): host backup of the prefill, hot buffer, bounds."""
+        req = int(req_pool_idx)
+        n = int(prefill_len)
+        idx = prefill_indices.to(device=self.device, dtype=torch.int32).contiguous()
+        host_idx = self.host_allocator.alloc(n)
+        host_idx_dev = host_idx.to(self.device)
+        self.req_to_host_pool[req, :n] = host_idx_dev.to(torch.int32)
+        n_dev = min(n, self.device_buffer_size)
+        kb = [token_to_kv_pool.get_key_buffer(layer) for layer in range(self.num_layers)]
+        vb = [token_to_kv_pool.get_value_buffer(layer) for layer in range(self.num_layers)]
+        src_arr, keep = _lib.ptr_array([t.data_ptr() for t in kb + vb])
+        stride = kb[0].stride(0) * kb[0].element_size()
+        s = self._stream()
+        # all prefill rows -> host tier
+        check(self.lib.qq_copy_rows(src_arr, self._host_ptrs[0], 2 * self.num_layers, stride, self.row_bytes,
+                                    self.row_bytes, idx.data_ptr(), 0, host_idx_dev.data_ptr(), 1, n, s),
+              "admit_request host copy")
+        # positions [0, n_dev) -> slots [0, n_dev) of the hot buffer
+        dev_rows = self.req_to_device_buffer[req, :n_dev].contiguous()
+        check(self.lib.qq_copy_rows(src_arr, self._dev_ptrs[0], 2 * self.num_layers, stride, self.row_bytes,
+                                    self.row_bytes, idx.data_ptr(), 0, dev_rows.data_ptr(), 1, n_dev, s),
+              "admit_request device copy")
+        check(self.lib.qq_hisparse_admit_layout(self._hs, req, s), "admit_request layout")
+        q = self.quest
+        q.update_prefill_representations_all_layers(req, kb[q.start_layer:q.end_layer], idx)
+        self._skip_first_backup[req] = True
+        del keep
+
+    # -------------------------------------------------- [H2] per decode step
+
+    def newest_slot(self, seq_lens: torch.Tensor) -> torch.Tensor:
+        return (seq_lens.long() - 1).clamp(max=self.device_buffer_size)
+
+    def prepare_decode_step(self, req_pool_indices: torch.Tensor, seq_lens: torch.Tensor) -> None:
+        """[H2] (coordinator.py:183-215): fold the previous token's key into the bounds, back it up."""
+        self.check_errors()
+        backup_reqs: list[int] = []
+        backup_pos: list[int] = []
+        for req, seq_len in zip(req_pool_indices.tolist(), seq_lens.tolist(), strict=True):
+            if self._skip_first_backup[req]:
+                self._skip_first_backup[req] = False
+                continue
+            backup_reqs.append(req)
+            backup_pos.append(seq_len - 2)
+        if not backup_reqs:
+            return
+        buf = self.device_buffer_size
+        dev_locs_l = [r * (buf + 1) + min(p, buf) for r, p in zip(backup_reqs, backup_pos)]
+        host_idx = self.host_allocator.alloc(len(backup_reqs))
+        packed = torch.tensor([backup_reqs, backup_pos, dev_locs_l, host_idx.tolist()], dtype=torch.int64)
+        packed = packed.pin_memory().to(self.device, non_blocking=True)
+        reqs, prev_pos, dev_locs, host_dev = packed[0], packed[1], packed[2], packed[3]
+        q = self.quest
+        q.decode_step(QQ_STEP_FOLD | QQ_STEP_FINALIZE, reqs, None, None, rows=dev_locs,
+                      k_ptrs=self._dev_k_ptrs[0], kv_dtype=dtype_code(self.dtype),
+                      k_row_stride=self.kv_heads * self.head_dim)
+        self.req_to_host_pool[reqs, prev_pos] = host_dev.to(torch.int32)
+        check(self.lib.qq_copy_rows(self._dev_ptrs[0], self._host_ptrs[0], 2 * self.num_layers, self.row_bytes,
+                                    self.row_bytes, self.row_bytes, dev_locs.data_ptr(), 1, host_dev.data_ptr(),
+                                    1, len(backup_reqs), self._stream()),
+              "eager host backup")
+
+    def write_new_token(self, layer_id, req_pool_indices, seq_lens, k, v) -> None:
+        """``set_kv_buffer`` redirected into the hot buffer (coordinator.py:217-228)."""
+        locs = self.req_to_device_buffer[req_pool_indices.long(), self.newest_slot(seq_lens)]
+        self.device_k[layer_id][locs] = k.to(self.device_k[layer_id].dtype)
+        self.device_v[layer_id][locs] = v.to(self.device_v[layer_id].dtype)
+
+    # -------------------------------------------------- [H3] swap-in
+
+    def swap_in(self, reqs, seq_lens, positions, layer_id, rows_out) -> None:
+        """One ``qq_hisparse_swap_in`` launch writing int32 rows into ``rows_out``."""
+        bs = int(reqs.shape[0])
+        batch = _lib.QQBatch(reqs.data_ptr(), seq_lens.data_ptr(), bs)
+        rc = self.lib.qq_hisparse_swap_in(
+            self._hs, int(layer_id), batch, positions.data_ptr(), rows_out.data_ptr(),
+            host_device_pointer(self.host_k[layer_id]), host_device_pointer(self.host_v[layer_id]),
+            self.device_k[layer_id].data_ptr(), self.device_v[layer_id].data_ptr(), self.row_bytes,
+            self._err.ptr(), self._stream(),
+        )
+        check(rc, "swap_in_selected_pages")
+
+    def swap_in_selected_pages(self, req_pool_indices, seq_lens, top_k_result, layer_id) -> torch.Tensor:
+        """[H3] (coordinator.py:232-257): ``[bs, top_k]`` int64 device rows, ``-1`` padded.
+
+        Errors (buffer too small, missing host backup) raise here, as in the
+        reference; this synchronizes the stream.
+        """
+        dev = self.device
+        reqs = req_pool_indices.to(device=dev, dtype=torch.int64).contiguous()
+        seq = seq_lens.to(device=dev, dtype=torch.int64).contiguous()
+        pos = top_k_result.to(device=dev, dtype=torch.int32).contiguous()
+        if pos.shape[1] != self.top_k:
+            full = torch.zeros((pos.shape[0], self.top_k), dtype=torch.int32, device=dev)
+            full[:, : pos.shape[1]] = pos
+            pos = full
+        rows = torch.empty((reqs.shape[0], self.top_k), dtype=torch.int32, device=dev)
+        self.swap_in(reqs, seq, pos, layer_id, rows)
+        torch.cuda.current_stream(dev).synchronize()
+        self.check_errors(f"(layer {layer_id})")
+        return rows.to(torch.int64)
+
+    # -------------------------------------------------- [H4] release
+
+    def request_finished(self, req_pool_idx: int) -> None:
+        """[H4] (coordinator.py:308-316)."""
+        req = int(req_pool_idx)
+        host_idx = self.req_to_host_pool[req].cpu()
+        self.host_allocator.free(host_idx[host_idx >= 0].to(torch.int64))
+        check(self.lib.qq_hisparse_reset(self._hs, req, self._stream()), "request_finished")
+        self._skip_first_backup[req] = False
+        self.quest.invalidate_request(req)
+
+    # -------------------------------------------------- introspection
+
+    def device_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (*self.device_k, *self.device_v))
+
+    def host_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in {id(t): t for t in self.host_k + self.host_v}.values())
+
+
+_ = ctypes

@@ -1,0 +1,82 @@
+"""The C-ABI library loads without a GPU and exports exactly what include/qquest.h declares (CPU)."""
+
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import pytest
+
+from qwenquest_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "qquest.h"
+
+
+def declared_functions() -> set[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return set(re.findall(r"^\s*(?:const\s+)?\w+\s*\**\s*(qq_\w+)\s*\(", text, flags=re.M))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not _lib.LIB_PATH.exists():
+        import __graft_entry__
+
+        __graft_entry__.build()
+    return _lib.load()
+
+
+def test_header_declares_the_bound_functions():
+    assert declared_functions() == set(_lib.SIGNATURES), (
+        declared_functions() ^ set(_lib.SIGNATURES)
+    )
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_introspection_calls_need_no_gpu(lib):
+    assert b"sm_100a" in lib.qq_version()
+    assert lib.qq_status_string(_lib.QQ_ERR_INVALID) == b"invalid argument"
+    ws = lib.qq_workspace_bytes(64, 2048, 32, 128)
+    # three counter arrays + attention partials of 64 requests x 16 chunks x 32 heads x (128 + 2) floats
+    assert ws >= 3 * 4 * _lib.QQ_MAX_BS + 4 * 64 * 16 * 32 * 130
+
+
+def test_argument_errors_are_reported_without_touching_a_device(lib):
+    st = _lib.QQQuestState()
+    assert lib.qq_quest_init_storage(st, None) == _lib.QQ_ERR_INVALID
+    assert lib.qq_quest_invalidate(None, 0, None) == _lib.QQ_ERR_INVALID
+    assert lib.qq_copy_rows(None, None, 0, 0, 0, 0, None, 0, None, 0, 0, None) == _lib.QQ_ERR_INVALID
+    with pytest.raises(ValueError):
+        _lib.check(_lib.QQ_ERR_INVALID, "probe")
+
+
+def test_device_error_bits_map_to_reference_exceptions():
+    with pytest.raises(RuntimeError):
+        _lib.raise_device_error(_lib.QQ_DEV_ERR_CAPACITY)
+    with pytest.raises(AssertionError):
+        _lib.raise_device_error(_lib.QQ_DEV_ERR_NO_HOST_BACKUP)
+    with pytest.raises(RuntimeError):
+        _lib.raise_device_error(_lib.QQ_DEV_ERR_TIMEOUT)
+    _lib.raise_device_error(0)
+
+
+def test_no_cpu_fallback():
+    """The product refuses to run without a CUDA device instead of computing on the CPU."""
+    import torch
+
+    from qwenquest_b200.quest import QuestAlgorithm
+
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    with pytest.raises(ValueError):
+        QuestAlgorithm(top_k=64, page_size=16, device="cpu")
+
+
+def test_package_does_not_import_the_oracle():
+    root = Path(__file__).resolve().parents[1] / "qwenquest_b200"
+    for p in root.rglob("*.py"):
+        assert "oracle" not in re.findall(r"^\s*(?:from|import)\s+(\w+)", p.read_text(), flags=re.M), p
