@@ -1,0 +1,481 @@
+"""Quest sparse-decode benchmark (benchmark config 1) — one JSON line on rank 0.
+
+Workload (per GPU): 64 requests, each with a 32 768-token prefix (512 complete
+pages of 64), Qwen3-30B-A3B attention geometry (32 query / 4 KV heads,
+head_dim 128, bf16), 48 layers, Quest top_k 2048 (31 pages + recent 64).  A
+*step* is one decode step through the drop-in backend's public interface:
+``init_forward_metadata`` (bounds fold of the previous token for all 48
+layers) then ``forward`` for each of the 48 layers (new K/V write + GQA mean
++ page scores + top-k + req_to_token translation + split-K sparse
+attention).  Unit: layer-steps/s, a layer-step being one layer of decode for
+the whole 64-request batch; whole-job value = sum over ranks.
+
+The full KV of 48 layers x 64 x 32 768 tokens (206 GB) does not fit one
+B200, so ``RESIDENT`` physical KV buffers are aliased over the 48 layers
+(layer l reads buffer l % RESIDENT); Quest bounds are kept for all 48 layers.
+Every layer-step reads ~338 MB of distinct data (far beyond the 126 MB L2),
+so aliasing changes no byte counts.  Inputs are synthetic (seeded N(0,1)
+scaled per channel by LogNormal(0, 0.5)); no dataset exists for this path.
+
+``--impl reference`` times the CPU oracle (the reference algorithm restated in
+numpy) on the host cores on a bounded sample of the same workload.
+Multi-GPU: one process per GPU (torchrun); requests are sharded per GPU with
+no collective on the hot path (weak scaling: 64 requests per GPU).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+H, KV, D = 32, 4, 128
+TOP_K, PAGE = 2048, 64
+LAYERS = 48
+N_REQ = 64
+PREFIX = 32768
+RESIDENT = 4
+METRIC = "Quest sparse-decode layer-steps/sec per GPU and box"
+UNIT = "layer-steps/s"
+
+# bytes per request-layer of the long-request layer step (algorithmic):
+# q 8192 + new K/V 2048 + bounds append 4096 + positions 8192 + req_to_token 8192
+# + K/V gather 2048 rows x 2048 B + output 8192, plus 2048 B per candidate page
+BYTES_FIXED = 8192 + 2048 + 4096 + 8192 + 8192 + 2048 * 2048 + 8192
+ATTN_BYTES_PER_REQ = 8192 + 8192 + 2048 * 2048 + 8192  # q + rows + K/V rows + out
+
+
+def layer_step_bytes(candidate_pages: int, n_req: int = N_REQ) -> int:
+    return n_req * (BYTES_FIXED + 2048 * candidate_pages)
+
+
+# --------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# --------------------------------------------------------------------------- setup
+
+
+class _Pool:
+    """``MHATokenToKVPool`` whose 48 layer buffers alias ``RESIDENT`` physical ones."""
+
+    def __init__(self, k_phys, v_phys, layers):
+        self.k_buffer = [k_phys[i % len(k_phys)] for i in range(layers)]
+        self.v_buffer = [v_phys[i % len(v_phys)] for i in range(layers)]
+        self.num_layers = layers
+        self.kv_heads, self.head_dim = KV, D
+        self.dtype = torch.bfloat16
+        self.device = k_phys[0].device
+        self.size = k_phys[0].shape[0] - 1
+
+    def get_key_buffer(self, i):
+        return self.k_buffer[i]
+
+    def get_value_buffer(self, i):
+        return self.v_buffer[i]
+
+    def get_kv_buffer(self, i):
+        return self.k_buffer[i], self.v_buffer[i]
+
+    def set_kv_buffer(self, i, loc, k, v):
+        self.k_buffer[i][loc.long()] = k.to(self.dtype)
+        self.v_buffer[i][loc.long()] = v.to(self.dtype)
+
+
+def build_config1(dev, total_steps: int, seed: int, n_req: int = N_REQ, prefix: int = PREFIX,
+                  layers: int = LAYERS, resident: int = RESIDENT):
+    from qwenquest_b200.backends import B200QuestOnlyBackend
+    from qwenquest_b200.memory import ReqToTokenPool
+    from qwenquest_b200.workloads import fill_rows_normal_, torch_generator
+
+    max_ctx = ((prefix + total_steps + 1 + PAGE - 1) // PAGE) * PAGE
+    rows = n_req * max_ctx + 1
+    gen = torch_generator(dev, seed)
+    k_phys, v_phys = [], []
+    for r in range(resident):
+        scale = torch.exp(0.5 * torch.randn(KV, D, generator=gen, device=dev))
+        kb = torch.empty((rows, KV, D), dtype=torch.bfloat16, device=dev)
+        vb = torch.empty((rows, KV, D), dtype=torch.bfloat16, device=dev)
+        fill_rows_normal_(kb, scale, gen)
+        fill_rows_normal_(vb, scale, gen)
+        k_phys.append(kb)
+        v_phys.append(vb)
+    pool = _Pool(k_phys, v_phys, layers)
+    r2t = ReqToTokenPool(n_req, max_ctx, dev)
+    # request i, position p -> row 1 + i * max_ctx + p (future decode positions pre-mapped)
+    r2t.req_to_token.copy_(
+        (1 + torch.arange(n_req, device=dev)[:, None] * max_ctx + torch.arange(max_ctx, device=dev)[None])
+        .to(torch.int32))
+    backend = B200QuestOnlyBackend(r2t, pool, {"algorithm": "quest", "top_k": TOP_K, "quest_page_size": PAGE})
+    q = backend.quest
+    # prefill bounds of every request for the resident buffers, copied to their aliases
+    for r in range(min(resident, layers)):
+        for i in range(n_req):
+            q.update_prefill_representations(r, i, k_phys[r], r2t.req_to_token[i, :prefix])
+    for layer in range(resident, layers):
+        q.page_k_bounds[layer].copy_(q.page_k_bounds[layer % resident])
+        q.running_k_min[layer].copy_(q.running_k_min[layer % resident])
+        q.running_k_max[layer].copy_(q.running_k_max[layer % resident])
+    q.running_token_count.fill_(prefix % PAGE)
+    q.running_page_idx.fill_(prefix // PAGE)
+    backend._skip_first_decode_update.fill_(1)  # prefill covered the last prompt token
+    # per-layer decode inputs
+    qs = torch.randn((layers, n_req, H, D), generator=gen, device=dev).to(torch.bfloat16)
+    ks = torch.randn((layers, n_req, KV, D), generator=gen, device=dev).to(torch.bfloat16)
+    vs = torch.randn((layers, n_req, KV, D), generator=gen, device=dev).to(torch.bfloat16)
+    torch.cuda.synchronize(dev)
+    return backend, pool, r2t, max_ctx, (qs, ks, vs)
+
+
+def make_batches(dev, backend, pool, r2t, max_ctx, total_steps, n_req=N_REQ, prefix=PREFIX):
+    from types import SimpleNamespace
+
+    from qwenquest_b200.batch import ForwardBatch, ForwardMode
+
+    reqs = torch.arange(n_req, dtype=torch.int64, device=dev)
+    batches = []
+    for s in range(total_steps):
+        pos = torch.full((n_req,), prefix + s, dtype=torch.int64, device=dev)
+        out_loc = 1 + reqs * max_ctx + pos
+        batches.append(ForwardBatch(
+            forward_mode=ForwardMode.DECODE, input_ids=torch.zeros(n_req, dtype=torch.int64, device=dev),
+            positions=pos, req_pool_indices=reqs, seq_lens=pos + 1, out_cache_loc=out_loc,
+            req_to_token_pool=r2t, token_to_kv_pool=pool, attn_backend=backend))
+    layers = [SimpleNamespace(layer_id=i, scaling=D ** -0.5, num_heads=H, num_kv_heads=KV, head_dim=D)
+              for i in range(pool.num_layers)]
+    return batches, layers
+
+
+def run_step(backend, batch, layers, qkv):
+    qs, ks, vs = qkv
+    backend.init_forward_metadata(batch)
+    out = None
+    for layer in layers:
+        li = layer.layer_id
+        out = backend.forward(qs[li], ks[li], vs[li], layer, batch)
+    return out
+
+
+# --------------------------------------------------------------------------- CPU baseline
+
+
+def cpu_baseline(sample_reqs: int = 2, min_seconds: float = 10.0, seed: int = 0) -> dict:
+    """The numpy oracle on a bounded sample of config 1: ``sample_reqs`` requests, one layer."""
+    from oracle.attention import decode_attention
+    from oracle.bf16 import round_bf16
+    from oracle.quest import OracleQuest
+
+    rng = np.random.default_rng(seed)
+    n = PREFIX + 1
+    scale = rng.lognormal(0, 0.5, size=(1, KV, D)).astype(np.float32)
+    ks = [round_bf16(rng.standard_normal((n, KV, D), dtype=np.float32) * scale) for _ in range(sample_reqs)]
+    vs = [round_bf16(rng.standard_normal((n, KV, D), dtype=np.float32) * scale) for _ in range(sample_reqs)]
+    q = round_bf16(rng.standard_normal((sample_reqs, H, D), dtype=np.float32))
+    oq = OracleQuest(TOP_K, PAGE)
+    oq.init_storage(0, 1, sample_reqs, n + PAGE, KV, D)
+    for i in range(sample_reqs):
+        oq.update_prefill_representations(0, i, ks[i], np.arange(PREFIX))
+    reqs = np.arange(sample_reqs)
+    seq = np.full(sample_reqs, n)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        # the per-step bounds fold of the previous token; counters reset so repetitions stay in range
+        oq.running_token_count[:] = 0
+        oq.running_page_idx[:] = PREFIX // PAGE
+        oq.update_decode_representations(0, reqs, np.stack([k[n - 2] for k in ks]), np.arange(sample_reqs))
+        oq.maybe_finalize_decode_representations(reqs)
+        oq.prepare_step(seq)
+        pos, actual = oq.retrieve_topk(q, 0, reqs, query_is_bf16=True)
+        for i in range(sample_reqs):
+            r = pos[i, : actual[i]].astype(np.int64)
+            decode_attention(q[i], ks[i][r], vs[i][r], D ** -0.5, out_bf16=True)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    per_req_layer = el / (reps * sample_reqs)
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {
+        "value": 1.0 / (per_req_layer * N_REQ),
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{reps} repetitions x {sample_reqs} requests x 1 layer of config 1 (numpy oracle, "
+                  f"BLAS threads up to {threads}), scaled to the 64-request layer-step",
+        "ms_per_request_layer": per_req_layer * 1e3,
+    }
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# --------------------------------------------------------------------------- main
+
+
+def load_profile_traffic() -> float | None:
+    p = ROOT / "profiles" / "traffic.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["sparse_decode_attention"]["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--requests", type=int, default=N_REQ, help="requests per GPU (profiling cases only)")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="layers (profiling cases only)")
+    ap.add_argument("--resident", type=int, default=RESIDENT, help="physical KV buffers")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        torch.set_num_threads(os.cpu_count() or 1)
+        t0 = time.perf_counter()
+        steps = []
+        for _ in range(args.warmup + args.steps):
+            steps.append(cpu_baseline(min_seconds=max(1.0, args.cpu_seconds / max(1, args.steps))))
+        timed = steps[args.warmup:]
+        value = statistics.mean(s["value"] for s in timed)
+        cb = dict(timed[0])
+        cb["value"] = value
+        line = {
+            "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * LAYERS / value,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "cpu_baseline": cb,
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "config": {"workload": "config1: 64 req x 32768 ctx, 48 layers, Quest top_k 2048 / page 64",
+                       "cpu": cpu_model(), "wall_s": time.perf_counter() - t0},
+        }
+        print(json.dumps(line))
+        return
+
+    if world > 1:
+        torch.distributed.init_process_group(
+            "nccl", timeout=__import__("datetime").timedelta(seconds=120),
+            device_id=torch.device("cuda", local_rank))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    total = args.warmup + args.steps
+    # two passes of the timed steps: value (inputs resident) and e2e (host inputs)
+    n_req, n_layers = args.requests, args.layers
+    backend, pool, r2t, max_ctx, qkv = build_config1(dev, 2 * total + 1, args.seed + 1000 * rank, n_req=n_req,
+                                                     layers=n_layers, resident=min(args.resident, n_layers))
+    batches, layers = make_batches(dev, backend, pool, r2t, max_ctx, 2 * total + 1, n_req=n_req)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    # ---- value: device-resident inputs
+    for s in range(args.warmup):
+        run_step(backend, batches[s], layers, qkv)
+    barrier()
+    backend.kernel_events = {}
+    clocks = ClockSampler(dev.index if world == 1 else local_rank)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for s in range(args.warmup, total):
+        run_step(backend, batches[s], layers, qkv)
+    end.record()
+    barrier()
+    clock_info = clocks.stop()
+    ms = start.elapsed_time(end)
+    kev = backend.kernel_events
+    backend.kernel_events = None
+    kernel_ms = {k: statistics.mean(a.elapsed_time(b) for a, b in v) for k, v in kev.items()}
+    launches = sum(len(v) for v in kev.values())
+    backend.check_errors()
+
+    # ---- e2e: host (pinned) inputs copied in, every layer's output copied out, each step
+    qs, ks, vs = qkv
+    hq, hk, hv = (t.cpu().pin_memory() for t in (qs, ks, vs))
+    hout = torch.empty((n_layers, n_req, H * D), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = torch.empty_like(qs), torch.empty_like(ks), torch.empty_like(vs)
+    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for s in range(total, total + args.warmup):
+        run_step(backend, batches[s], layers, qkv)
+    barrier()
+    e2e_start.record()
+    for s in range(total + args.warmup, 2 * total):
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        b = batches[s]
+        backend.init_forward_metadata(b)
+        for layer in layers:
+            li = layer.layer_id
+            o = backend.forward(dq[li], dk[li], dv[li], layer, b)
+            hout[li].copy_(o, non_blocking=True)
+    e2e_end.record()
+    barrier()
+    e2e_ms = e2e_start.elapsed_time(e2e_end)
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+
+    c = PREFIX // PAGE + 0  # candidate pages at the first timed step (F = 512 while seq_len < 32832)
+    value = world * n_layers * args.steps / (ms / 1e3)
+    e2e_value = world * n_layers * args.steps / (e2e_ms / 1e3)
+    peak, peak_kind = measured_peaks()
+    attn_ms = kernel_ms.get("sparse_decode_attention")
+    achieved = n_req * ATTN_BYTES_PER_REQ / (attn_ms / 1e3) / 1e9 if attn_ms else None
+    traffic = load_profile_traffic()
+    step_bytes = layer_step_bytes(c, n_req)
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) x LogNormal(0,0.5) per-channel K/V, N(0,1) q)",
+        "config": {
+            "workload": "config1: 64 requests/GPU x 32768-token prefix, 48 layers, Quest top_k 2048 / page 64, "
+                        "Qwen3-30B-A3B attention (32q/4kv x 128, bf16), quest mode",
+            "requests_per_gpu": n_req, "layers": n_layers, "resident_kv_layers": min(args.resident, n_layers),
+            "l2": "inputs larger than L2 (each layer-step reads ~338 MB of distinct data)",
+            "layer_step_bytes": step_bytes,
+            "layer_step_gbs": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 1e9,
+            "layer_step_frac_of_peak": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 1e9 / peak,
+            "kernel_ms": kernel_ms,
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "sparse_decode_attention",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak if achieved else None,
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": n_req * ATTN_BYTES_PER_REQ,
+            "peak_kind": peak_kind,
+        },
+        "clocks": clock_info,
+        "gpu_launches": launches,
+        "e2e": {
+            "value": e2e_value,
+            "unit": UNIT,
+            "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in (hq, hk, hv))),
+            "d2h_bytes_per_step": int(hout.numel() * hout.element_size()),
+        },
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        line["cpu_baseline"] = cpu_baseline(min_seconds=args.cpu_seconds)
+        line["config"]["cpu"] = cpu_model()
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -130,6 +130,23 @@ class _QuestDecodeMixin:
         self._step_seq: torch.Tensor | None = None
         self._max_reqs = max_reqs
         self.lib = _lib.load()
+        #: when a dict, every launch of the decode path records a (start, end)
+        #: CUDA event pair under its kernel name (benchmark instrumentation)
+        self.kernel_events: dict[str, list] | None = None
+
+    def _ev_begin(self):
+        if self.kernel_events is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(self.device))
+        return ev
+
+    def _ev_end(self, name: str, start) -> None:
+        if start is None:
+            return
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(self.device))
+        self.kernel_events.setdefault(name, []).append((start, ev))
 
     def _begin_step(self, batch) -> None:
         self._step_reqs = batch.req_pool_indices.to(device=self.device, dtype=torch.int64).contiguous()
@@ -156,6 +173,7 @@ class _QuestDecodeMixin:
         out = torch.empty((bs, heads * dim), dtype=q3.dtype, device=self.device)
         ws = self._workspace(heads, dim)
         batch = _lib.QQBatch(reqs.data_ptr(), seq.data_ptr(), bs)
+        ev = self._ev_begin()
         rc = self.lib.qq_sparse_decode_attention(
             batch, self.quest.top_k, q3.data_ptr(), dtype_code(q3.dtype), heads, self.quest.kv_heads, dim,
             q3.stride(0), rows.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), k_pool.stride(0),
@@ -163,6 +181,7 @@ class _QuestDecodeMixin:
             ws.data_ptr(), ws.numel(), stream_of(self.device),
         )
         check(rc, "sparse decode attention")
+        self._ev_end("sparse_decode_attention", ev)
         return out
 
     def _new_token(self, k, v, k_dst, v_dst, dst_rows, buf) -> _lib.QQNewToken:
@@ -220,11 +239,13 @@ class B200QuestOnlyBackend(_QuestDecodeMixin, AttentionBackend):
             self.check_errors()
             self._begin_step(batch)
             # [Q3] fold the previous token (seq_len - 2) into all layers' running bounds (quest_only.py:84-97)
+            ev = self._ev_begin()
             self.quest.decode_step(
                 QQ_STEP_FOLD | QQ_STEP_FINALIZE, self._step_reqs, self._step_seq, None,
                 skip_flags=self._skip_first_decode_update, req_to_token=self.req_to_token,
                 k_ptrs=self._k_layers[0], kv_dtype=self._kv_dtype, k_row_stride=self._k_row_stride,
             )
+            self._ev_end("quest_decode_step", ev)
 
     # ----------------------------------------------------------------- prefill
 
@@ -260,8 +281,10 @@ class B200QuestOnlyBackend(_QuestDecodeMixin, AttentionBackend):
         nt = self._new_token(kk, vv, k_buf, v_buf, dst, 0)
         table = _lib.QQTokenTable(self.req_to_token.data_ptr(), self.req_to_token.stride(0))
         # [Q6] + [Q7] translation + new K/V write, one launch
+        ev = self._ev_begin()
         self.quest.select(q3, li, reqs, seq, self._positions, self._actual, translate=table,
                           rows=self._rows, new_token=nt)
+        self._ev_end("quest_retrieve_topk", ev)
         # [Q7] attention over exactly those rows (duplicates kept)
         return self._attend(q3, layer, reqs, seq, self._rows, k_buf, v_buf)
 
@@ -345,9 +368,13 @@ class B200QuestHiSparseBackend(_QuestDecodeMixin, AttentionBackend):
         vv = v.to(v_dev.dtype).reshape(bs, -1).contiguous()
         # 1. new K/V into the newest slot, 2. [Q6] selection — one launch
         nt = self._new_token(kk, vv, k_dev, v_dev, None, coord.device_buffer_size)
+        ev = self._ev_begin()
         self.quest.select(q3, li, reqs, seq, self._positions, self._actual, new_token=nt)
+        self._ev_end("quest_retrieve_topk", ev)
         # 3. [H3] positions -> hot-buffer rows (misses copied from the host tier)
+        ev = self._ev_begin()
         coord.swap_in(reqs, seq, self._positions, li, self._rows)
+        self._ev_end("hisparse_swap_in", ev)
         # 4. [Q7] attention over the hot buffer
         return self._attend(q3, layer, reqs, seq, self._rows, k_dev, v_dev)
 

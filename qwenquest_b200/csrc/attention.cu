@@ -98,6 +98,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return (h << 16) | l;
 }
 
+// Packs bf16(lo), bf16(hi) and returns the rounded values as floats.
+__device__ __forceinline__ uint32_t pack_bf16x2_split(float lo, float hi, float& lo_r, float& hi_r) {
+  const uint32_t l = f32_to_bf16_bits(lo), h = f32_to_bf16_bits(hi);
+  lo_r = bf16_bits_to_f32(l);
+  hi_r = bf16_bits_to_f32(h);
+  return (h << 16) | l;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
 #define kNegInf (-__int_as_float(0x7f800000))
@@ -259,9 +267,17 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
           acc[mt][2] *= al_a;
           acc[mt][3] *= al_b;
         }
-        // ---- P^T fragments (rows x heads -> heads x rows) and O^T += V^T . P^T
-        const uint32_t pb0 = movmatrix_trans(pack_bf16x2(p00, p01));
-        const uint32_t pb1 = movmatrix_trans(pack_bf16x2(p10, p11));
+        // ---- P^T fragments (rows x heads -> heads x rows) and O^T += V^T . P^T.
+        // P is split into bf16 hi + lo parts (two MMAs per tile), so the
+        // weights carry ~16 mantissa bits and the fp32 result tracks an fp32
+        // softmax-weighted sum to ~1e-5 relative.
+        float h00, h01, h10, h11;
+        const uint32_t ph0 = pack_bf16x2_split(p00, p01, h00, h01);
+        const uint32_t ph1 = pack_bf16x2_split(p10, p11, h10, h11);
+        const uint32_t pb0 = movmatrix_trans(ph0);
+        const uint32_t pb1 = movmatrix_trans(ph1);
+        const uint32_t pl0 = movmatrix_trans(pack_bf16x2(p00 - h00, p01 - h01));
+        const uint32_t pl1 = movmatrix_trans(pack_bf16x2(p10 - h10, p11 - h11));
         const int j = lane >> 3, r = lane & 7;
         const uint32_t vaddr =
             smem_u32(sv + (half * 16 + (j >> 1) * 8 + r) * kPitch + h * (kD * 2) + (j & 1) * 16);
@@ -270,6 +286,7 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
           uint32_t a0, a1, a2, a3;
           ldmatrix_x4_trans(a0, a1, a2, a3, vaddr + mt * 32);
           mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+          mma_bf16_16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
         }
       }
       __syncwarp();

@@ -1,8 +1,8 @@
 """Sparse decode attention kernel against the oracle's ``decode_attention`` (GPU).
 
-Tolerances: 2e-2 absolute for bf16 outputs, 1e-5 for fp32 (the contract of
-the reference's ``decode_attention``, ``attention/ops.py:48-66``: fp32
-scores, softmax and accumulation; duplicates counted).
+Tolerances: the kernel's bf16 output must be within 2e-2 absolute of the
+oracle's fp32 attention result (the value the reference computes before its
+final cast to bf16, ``attention/ops.py:60-66``); fp32 outputs within 1e-5.
 """
 
 from __future__ import annotations
@@ -33,13 +33,12 @@ def _check(q, k, v, rows, seq, top_k, atol):
     scaling = q.shape[-1] ** -0.5
     out = sparse_decode_attention(q.cuda(), k.cuda(), v.cuda(), rows.cuda(), seq.cuda(), top_k, scaling)
     out = out.float().cpu().numpy()
-    bf16 = q.dtype == torch.bfloat16
     kn, vn, qn = k.float().numpy(), v.float().numpy(), q.float().numpy()
     worst = 0.0
     for b in range(q.shape[0]):
         n = int(min(seq[b], top_k))
         r = rows[b, :n].long().numpy()
-        ref = decode_attention(qn[b], kn[r], vn[r], scaling, out_bf16=bf16)
+        ref = decode_attention(qn[b], kn[r], vn[r], scaling, out_bf16=False)
         worst = max(worst, float(np.abs(out[b] - ref).max()))
     assert worst <= atol, worst
     return worst
