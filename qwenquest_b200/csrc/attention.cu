@@ -1,19 +1,23 @@
 // [Q7] Split-K sparse decode attention over an explicit row list.
 //
 // Fast path (bf16, 4 KV heads, head_dim 128, 8 query heads per KV head):
-// a persistent kernel, one block per SM.  Work items are (request, chunk of
-// 128 rows).  Warp 8 is the producer: for each stage of 32 rows its lanes
-// issue one 1 KiB cp.async.bulk for the K row and one for the V row (the
-// whole row: all 4 KV heads), completing on the stage's mbarrier; rows land
-// at a 1040-byte pitch so ldmatrix reads are bank-conflict free.  Warps 0-7
-// are consumers, warp w owning KV head w%4 and half w/4 of every stage:
+// a persistent kernel, one 256-thread block per SM.  Work items are
+// (request, chunk of 128 rows), assigned round-robin; a block walks the
+// 32-row stages of its items as one stream through a 3-slot shared-memory
+// ring, so the gather of stage g+2 is in flight while stage g is computed,
+// across item boundaries.  The gather is done by all 8 warps with 16-byte
+// cp.async.cg copies (a warp moves 512 contiguous bytes of one row per
+// instruction; rows past the end are zero-filled by the copy), 4096 copies
+// per 64 KiB stage, so every SM keeps ~128 KiB of independent requests in
+// flight.  Rows land at a 1040-byte pitch: ldmatrix reads are bank-conflict
+// free.  Warp w computes KV head w%4 on half w/4 of every stage:
 //   S^T[16 rows x 8 heads] = K[16 x 128] . Q^T[128 x 8]   (8 x mma m16n8k16)
 //   online softmax in fp32 (exp2 domain), P^T via movmatrix.trans
-//   O^T[128 x 8] += V^T[128 x 16] . P^T[16 x 8]          (8 x mma m16n8k16)
+//   O^T[128 x 8] += V^T[128 x 16] . P^T[16 x 8]          (P as bf16 hi + lo: 16 mma)
 // The two halves of a head merge through shared memory at the end of the
 // item; chunks of one request merge in the last block to finish (arrival
-// counter in the workspace).  Per row the kernel reads 2 KiB and does 16 K
-// FMA-equivalents on the tensor cores, so it is HBM-bound.
+// counter in the workspace).  Per row the kernel reads 2 KiB, so it is
+// HBM-bound.
 //
 // Generic path (any head_dim / group / fp32): one block per (request, KV
 // head), scores in shared memory, two-pass softmax, fp32 FMA.
@@ -30,17 +34,17 @@ constexpr int kD = 128;
 constexpr int kKV = 4;
 constexpr int kG = 8;
 constexpr int kH = kKV * kG;
-constexpr int kRowBytes = kKV * kD * 2;    // 1024
+constexpr int kRowBytes = kKV * kD * 2;    // 1024: one K (or V) row, all KV heads
 constexpr int kPitch = kRowBytes + 16;     // 1040
 constexpr int kToks = 32;                  // rows per stage
-constexpr int kStages = 3;
+constexpr int kSlots = 3;                  // stages resident in shared memory
 constexpr int kChunk = kAttnChunk;         // 128 rows per work item
-constexpr int kConsumerWarps = 8;
-constexpr int kThreadsFast = (kConsumerWarps + 1) * 32;
-constexpr int kStageBytes = 2 * kToks * kPitch;  // K tile + V tile
+constexpr int kWarpsFast = 8;
+constexpr int kThreadsFast = kWarpsFast * 32;
+constexpr int kSlotBytes = 2 * kToks * kPitch;  // K tile + V tile
 constexpr int kMergeFloats = kKV * kG * kD;     // 4096
-constexpr size_t kSmemFast =
-    (size_t)kStages * kStageBytes + sizeof(float) * (kMergeFloats + 2 * kKV * kG) + 2 * kStages * 8 + 16;
+constexpr int kCopiesPerThread = kToks * 2 * kRowBytes / 16 / kThreadsFast;  // 16
+constexpr size_t kSmemFast = (size_t)kSlots * kSlotBytes + sizeof(float) * (kMergeFloats + 2 * kKV * kG) + 16;
 
 struct AttnArgs {
   const int64_t* seq_lens;
@@ -108,202 +112,216 @@ __device__ __forceinline__ uint32_t pack_bf16x2_split(float lo, float hi, float&
 
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
+// 16-byte async copy global -> shared; src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 #define kNegInf (-__int_as_float(0x7f800000))
+
+// A position in a block's stream of stages: stage `sub` of work item `item`.
+struct Cursor {
+  int item;  // -1 before the first stage, >= total when exhausted
+  int sub;
+  int cnt;   // rows of the item
+  int base;  // first row (within the request's list) of the item
+  int req;   // batch index
+};
 
 __device__ __forceinline__ int item_rows(const AttnArgs& a, int item, int& req, int& base) {
   req = item / a.max_chunks;
   const int c = item - req * a.max_chunks;
-  const int64_t L = a.seq_lens[req];
+  const int64_t L = __ldg(a.seq_lens + req);
   const int n = (int)(L < a.top_k ? L : a.top_k);
   base = c * kChunk;
   const int cnt = n - base;
   return cnt <= 0 ? 0 : (cnt < kChunk ? cnt : kChunk);
 }
 
+// Advance to the next stage of this block's stream; false when exhausted.
+__device__ __forceinline__ bool next_stage(const AttnArgs& a, Cursor& c, int total_items) {
+  if (c.item >= 0 && c.item < total_items && (c.sub + 1) * kToks < c.cnt) {
+    ++c.sub;
+    return true;
+  }
+  int item = c.item < 0 ? (int)blockIdx.x : c.item + (int)gridDim.x;
+  for (; item < total_items; item += gridDim.x) {
+    int req, base;
+    const int cnt = item_rows(a, item, req, base);
+    if (cnt > 0) {
+      c.item = item;
+      c.sub = 0;
+      c.cnt = cnt;
+      c.base = base;
+      c.req = req;
+      return true;
+    }
+  }
+  c.item = total_items;
+  return false;
+}
+
+// Gather the 32 K and V rows of stage `c` into `slot` (all 256 threads,
+// kCopiesPerThread 16-byte copies each; a warp copies 512 contiguous bytes).
+__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Cursor& c, char* slot, int warp, int lane) {
+  const int r0 = c.base + c.sub * kToks;
+  const int ntok = min(kToks, c.cnt - c.sub * kToks);
+  int64_t my_row = 0;  // lane l holds the pool row of stage row l
+  if (lane < ntok) {
+    my_row = __ldg(a.rows + (int64_t)c.req * a.top_k + r0 + lane);
+    if (my_row < 0 || my_row >= a.num_rows) {
+      raise_error(a.err, QQ_DEV_ERR_BOUNDS);
+      my_row = 0;
+    }
+  }
+  const int sub_row = warp >> 2;           // 0/1: which of the two rows this warp copies per round
+  const int chunk = (warp & 3) * 32 + lane;  // 16-byte chunk within the 2 KiB (K | V) row
+  const bool is_v = chunk >= 64;
+  const int off = (chunk & 63) * 16;
+  const char* pool = is_v ? a.v_pool : a.k_pool;
+  char* dst0 = slot + (is_v ? kToks * kPitch : 0) + off;
+#pragma unroll
+  for (int k = 0; k < kCopiesPerThread; ++k) {
+    const int r = 2 * k + sub_row;
+    const int64_t row = __shfl_sync(0xffffffffu, my_row, r);
+    const bool valid = r < ntok;
+    cp_async_16(dst0 + r * kPitch, pool + row * a.row_stride_bytes + off, valid ? 16u : 0u);
+  }
+}
+
 __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) {
   extern __shared__ __align__(128) char smem[];
-  char* s_stage = smem;
-  float* s_merge = reinterpret_cast<float*>(smem + (size_t)kStages * kStageBytes);
-  float* s_mm = s_merge + kMergeFloats;  // [kKV][kG] m
-  float* s_ml = s_mm + kKV * kG;         // [kKV][kG] l
-  uint64_t* s_full = reinterpret_cast<uint64_t*>(s_ml + kKV * kG);
-  uint64_t* s_empty = s_full + kStages;
-  int* s_flag = reinterpret_cast<int*>(s_empty + kStages);
+  float* s_merge = reinterpret_cast<float*>(smem + (size_t)kSlots * kSlotBytes);
+  float* s_mm = s_merge + kMergeFloats;  // [kKV][kG] m of the second half
+  float* s_ml = s_mm + kKV * kG;         // [kKV][kG] l of the second half
+  int* s_flag = reinterpret_cast<int*>(s_ml + kKV * kG);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], kConsumerWarps);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-
-  const int total_items = a.bs * a.max_chunks;
-
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer
-    int stage = 0;
-    uint32_t ephase = 1;  // a fresh barrier's preceding phase counts as complete
-    for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
-      int req, base;
-      const int cnt = item_rows(a, item, req, base);
-      if (cnt == 0) continue;
-      const int32_t* rows = a.rows + (int64_t)req * a.top_k + base;
-      for (int s0 = 0; s0 < cnt; s0 += kToks) {
-        if (!mbar_wait(&s_empty[stage], ephase)) {
-          raise_error(a.err, QQ_DEV_ERR_TIMEOUT);
-          return;
-        }
-        const int ntok = min(kToks, cnt - s0);
-        char* sk = s_stage + (size_t)stage * kStageBytes;
-        char* sv = sk + kToks * kPitch;
-        if (ntok < kToks) {
-          if (lane >= ntok) {  // rows past the end: zero V so that 0 * V stays 0
-            uint4* z = reinterpret_cast<uint4*>(sv + lane * kPitch);
-            for (int w = 0; w < kRowBytes / 16; ++w) z[w] = make_uint4(0, 0, 0, 0);
-          }
-          fence_proxy_async_smem();
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&s_full[stage], (uint32_t)ntok * 2u * kRowBytes);
-        __syncwarp();
-        if (lane < ntok) {
-          int64_t row = rows[s0 + lane];
-          if (row < 0 || row >= a.num_rows) {
-            raise_error(a.err, QQ_DEV_ERR_BOUNDS);
-            row = 0;
-          }
-          bulk_g2s(sk + lane * kPitch, a.k_pool + row * a.row_stride_bytes, kRowBytes, &s_full[stage]);
-          bulk_g2s(sv + lane * kPitch, a.v_pool + row * a.row_stride_bytes, kRowBytes, &s_full[stage]);
-        }
-        if (++stage == kStages) {
-          stage = 0;
-          ephase ^= 1;
-        }
-      }
-    }
-    return;
-  }
-
-  // -------------------------------------------------------------- consumers
   const int h = warp & 3;      // KV head
   const int half = warp >> 2;  // which 16 rows of each stage
   const int gid = lane >> 2, tig = lane & 3;
-  int stage = 0;
-  uint32_t fphase = 0;
+  const int total_items = a.bs * a.max_chunks;
   const __nv_bfloat16* qbase = static_cast<const __nv_bfloat16*>(a.q);
 
-  for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
-    int req, base;
-    const int cnt = item_rows(a, item, req, base);
-    if (cnt == 0) continue;
-    const int chunk = base / kChunk;
-    const int nchunks = (int)(((a.seq_lens[req] < a.top_k ? a.seq_lens[req] : a.top_k) + kChunk - 1) / kChunk);
+  // prologue: put kSlots - 1 stages in flight
+  Cursor fc{-1, 0, 0, 0, 0}, cc{-1, 0, 0, 0, 0};
+#pragma unroll
+  for (int s = 0; s < kSlots - 1; ++s) {
+    if (next_stage(a, fc, total_items)) issue_stage(a, fc, smem + (size_t)s * kSlotBytes, warp, lane);
+    cp_async_commit();
+  }
 
-    // Q^T fragments of KV head h: B[k = d][n = query head g]
-    uint32_t qb[8][2];
-    {
-      const uint32_t* qrow =
-          reinterpret_cast<const uint32_t*>(qbase + (int64_t)req * a.q_stride + (int64_t)(h * kG + gid) * kD);
+  uint32_t qb[8][2];
+  float acc[8][4];
+  float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
+  int g = 0;
+  while (next_stage(a, cc, total_items)) {
+    cp_async_wait<kSlots - 2>();
+    __syncthreads();  // stage g visible to all; slot (g - 1) % kSlots free
+    if (next_stage(a, fc, total_items))
+      issue_stage(a, fc, smem + (size_t)((g + kSlots - 1) % kSlots) * kSlotBytes, warp, lane);
+    cp_async_commit();
+
+    if (cc.sub == 0) {
+      // Q^T fragments of KV head h: B[k = d][n = query head g]
+      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qbase + (int64_t)cc.req * a.q_stride +
+                                                               (int64_t)(h * kG + gid) * kD);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         qb[kk][0] = __ldg(qrow + (kk * 16 + 2 * tig) / 2);
         qb[kk][1] = __ldg(qrow + (kk * 16 + 8 + 2 * tig) / 2);
       }
-    }
-    float acc[8][4];
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
-    float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
-
-    for (int s0 = 0; s0 < cnt; s0 += kToks) {
-      if (!mbar_wait(&s_full[stage], fphase)) {
-        raise_error(a.err, QQ_DEV_ERR_TIMEOUT);
-        return;
-      }
-      const int ntok = min(kToks, cnt - s0);
-      const char* sk = s_stage + (size_t)stage * kStageBytes;
-      const char* sv = sk + kToks * kPitch;
-      const int t0 = half * 16 + gid, t1 = t0 + 8;
-      if (half * 16 < ntok) {
-        // ---- S^T = K . Q^T
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t kaddr = smem_u32(sk + (half * 16 + (lane & 15)) * kPitch + h * (kD * 2) + (lane >> 4) * 16);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          uint32_t a0, a1, a2, a3;
-          ldmatrix_x4(a0, a1, a2, a3, kaddr + kk * 32);
-          mma_bf16_16816(c, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
-        }
-        // ---- online softmax (exp2 domain); rows >= ntok are masked
-        const bool v0 = t0 < ntok, v1 = t1 < ntok;
-        const float s00 = v0 ? c[0] * a.scale_log2 : kNegInf;  // row t0, head 2tig
-        const float s01 = v0 ? c[1] * a.scale_log2 : kNegInf;  // row t0, head 2tig+1
-        const float s10 = v1 ? c[2] * a.scale_log2 : kNegInf;  // row t1, head 2tig
-        const float s11 = v1 ? c[3] * a.scale_log2 : kNegInf;  // row t1, head 2tig+1
-        float mx_a = fmaxf(s00, s10), mx_b = fmaxf(s01, s11);
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o));
-          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
-        }
-        const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-        const float al_a = mn_a == kNegInf ? 1.f : fast_exp2(m_a - mn_a);
-        const float al_b = mn_b == kNegInf ? 1.f : fast_exp2(m_b - mn_b);
-        const float p00 = mn_a == kNegInf ? 0.f : fast_exp2(s00 - mn_a);
-        const float p10 = mn_a == kNegInf ? 0.f : fast_exp2(s10 - mn_a);
-        const float p01 = mn_b == kNegInf ? 0.f : fast_exp2(s01 - mn_b);
-        const float p11 = mn_b == kNegInf ? 0.f : fast_exp2(s11 - mn_b);
-        m_a = mn_a;
-        m_b = mn_b;
-        l_a = l_a * al_a + p00 + p10;
-        l_b = l_b * al_b + p01 + p11;
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          acc[mt][0] *= al_a;
-          acc[mt][1] *= al_b;
-          acc[mt][2] *= al_a;
-          acc[mt][3] *= al_b;
-        }
-        // ---- P^T fragments (rows x heads -> heads x rows) and O^T += V^T . P^T.
-        // P is split into bf16 hi + lo parts (two MMAs per tile), so the
-        // weights carry ~16 mantissa bits and the fp32 result tracks an fp32
-        // softmax-weighted sum to ~1e-5 relative.
-        float h00, h01, h10, h11;
-        const uint32_t ph0 = pack_bf16x2_split(p00, p01, h00, h01);
-        const uint32_t ph1 = pack_bf16x2_split(p10, p11, h10, h11);
-        const uint32_t pb0 = movmatrix_trans(ph0);
-        const uint32_t pb1 = movmatrix_trans(ph1);
-        const uint32_t pl0 = movmatrix_trans(pack_bf16x2(p00 - h00, p01 - h01));
-        const uint32_t pl1 = movmatrix_trans(pack_bf16x2(p10 - h10, p11 - h11));
-        const int j = lane >> 3, r = lane & 7;
-        const uint32_t vaddr =
-            smem_u32(sv + (half * 16 + (j >> 1) * 8 + r) * kPitch + h * (kD * 2) + (j & 1) * 16);
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          uint32_t a0, a1, a2, a3;
-          ldmatrix_x4_trans(a0, a1, a2, a3, vaddr + mt * 32);
-          mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
-          mma_bf16_16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[stage]);
-      if (++stage == kStages) {
-        stage = 0;
-        fphase ^= 1;
-      }
+      for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+      m_a = m_b = kNegInf;
+      l_a = l_b = 0.f;
     }
 
-    // ---- per-thread l partials -> per-head sums
+    const int ntok = min(kToks, cc.cnt - cc.sub * kToks);
+    const char* sk = smem + (size_t)(g % kSlots) * kSlotBytes;
+    const char* sv = sk + kToks * kPitch;
+    const int t0 = half * 16 + gid, t1 = t0 + 8;
+    if (half * 16 < ntok) {
+      // ---- S^T = K . Q^T
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t kaddr = smem_u32(sk + (half * 16 + (lane & 15)) * kPitch + h * (kD * 2) + (lane >> 4) * 16);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4(a0, a1, a2, a3, kaddr + kk * 32);
+        mma_bf16_16816(c, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      }
+      // ---- online softmax (exp2 domain); rows >= ntok are masked
+      const bool v0 = t0 < ntok, v1 = t1 < ntok;
+      const float s00 = v0 ? c[0] * a.scale_log2 : kNegInf;  // row t0, head 2tig
+      const float s01 = v0 ? c[1] * a.scale_log2 : kNegInf;  // row t0, head 2tig+1
+      const float s10 = v1 ? c[2] * a.scale_log2 : kNegInf;  // row t1, head 2tig
+      const float s11 = v1 ? c[3] * a.scale_log2 : kNegInf;  // row t1, head 2tig+1
+      float mx_a = fmaxf(s00, s10), mx_b = fmaxf(s01, s11);
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
+      }
+      const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+      const float al_a = mn_a == kNegInf ? 1.f : fast_exp2(m_a - mn_a);
+      const float al_b = mn_b == kNegInf ? 1.f : fast_exp2(m_b - mn_b);
+      const float p00 = mn_a == kNegInf ? 0.f : fast_exp2(s00 - mn_a);
+      const float p10 = mn_a == kNegInf ? 0.f : fast_exp2(s10 - mn_a);
+      const float p01 = mn_b == kNegInf ? 0.f : fast_exp2(s01 - mn_b);
+      const float p11 = mn_b == kNegInf ? 0.f : fast_exp2(s11 - mn_b);
+      m_a = mn_a;
+      m_b = mn_b;
+      l_a = l_a * al_a + p00 + p10;
+      l_b = l_b * al_b + p01 + p11;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        acc[mt][0] *= al_a;
+        acc[mt][1] *= al_b;
+        acc[mt][2] *= al_a;
+        acc[mt][3] *= al_b;
+      }
+      // ---- P^T fragments (rows x heads -> heads x rows) and O^T += V^T . P^T.
+      // P is split into bf16 hi + lo parts (two MMAs per tile), so the
+      // weights carry ~16 mantissa bits and the fp32 result tracks an fp32
+      // softmax-weighted sum to ~1e-5 relative.
+      float h00, h01, h10, h11;
+      const uint32_t pb0 = movmatrix_trans(pack_bf16x2_split(p00, p01, h00, h01));
+      const uint32_t pb1 = movmatrix_trans(pack_bf16x2_split(p10, p11, h10, h11));
+      const uint32_t pl0 = movmatrix_trans(pack_bf16x2(p00 - h00, p01 - h01));
+      const uint32_t pl1 = movmatrix_trans(pack_bf16x2(p10 - h10, p11 - h11));
+      const int j = lane >> 3, r = lane & 7;
+      const uint32_t vaddr =
+          smem_u32(sv + (half * 16 + (j >> 1) * 8 + r) * kPitch + h * (kD * 2) + (j & 1) * 16);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4_trans(a0, a1, a2, a3, vaddr + mt * 32);
+        mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+        mma_bf16_16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
+      }
+    }
+    ++g;
+    if ((cc.sub + 1) * kToks < cc.cnt) continue;
+
+    // ------------------------------------------------------------ item epilogue
+    const int req = cc.req;
+    const int chunk = cc.base / kChunk;
+    const int64_t Lr = __ldg(a.seq_lens + req);
+    const int nchunks = (int)(((Lr < a.top_k ? Lr : a.top_k) + kChunk - 1) / kChunk);
+    float la = l_a, lb = l_b;
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
-      l_a += __shfl_xor_sync(0xffffffffu, l_a, o);
-      l_b += __shfl_xor_sync(0xffffffffu, l_b, o);
+      la += __shfl_xor_sync(0xffffffffu, la, o);
+      lb += __shfl_xor_sync(0xffffffffu, lb, o);
     }
-    // ---- merge the two halves of head h through shared memory
     float* mo = s_merge + h * (kG * kD);
     if (half == 1) {
 #pragma unroll
@@ -317,11 +335,11 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
       if (gid == 0) {
         s_mm[h * kG + 2 * tig] = m_a;
         s_mm[h * kG + 2 * tig + 1] = m_b;
-        s_ml[h * kG + 2 * tig] = l_a;
-        s_ml[h * kG + 2 * tig + 1] = l_b;
+        s_ml[h * kG + 2 * tig] = la;
+        s_ml[h * kG + 2 * tig + 1] = lb;
       }
     }
-    named_bar_sync(1, kConsumerWarps * 32);
+    __syncthreads();
     if (half == 0) {
       const float mo_a = s_mm[h * kG + 2 * tig], mo_b = s_mm[h * kG + 2 * tig + 1];
       const float lo_a = s_ml[h * kG + 2 * tig], lo_b = s_ml[h * kG + 2 * tig + 1];
@@ -330,7 +348,7 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
       const float fo_a = mo_a == kNegInf ? 0.f : fast_exp2(mo_a - M_a);
       const float fa_b = m_b == kNegInf ? 0.f : fast_exp2(m_b - M_b);
       const float fo_b = mo_b == kNegInf ? 0.f : fast_exp2(mo_b - M_b);
-      const float L_a = l_a * fa_a + lo_a * fo_a, L_b = l_b * fa_b + lo_b * fo_b;
+      const float L_a = la * fa_a + lo_a * fo_a, L_b = lb * fa_b + lo_b * fo_b;
       const int qh_a = h * kG + 2 * tig, qh_b = qh_a + 1;  // query heads of this thread
       if (nchunks == 1) {
         __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)req * a.out_stride;
@@ -338,8 +356,7 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
           const int d0 = mt * 16 + gid;
-          out[qh_a * kD + d0] =
-              __float2bfloat16_rn((acc[mt][0] * fa_a + mo[(2 * tig) * kD + d0] * fo_a) * inv_a);
+          out[qh_a * kD + d0] = __float2bfloat16_rn((acc[mt][0] * fa_a + mo[(2 * tig) * kD + d0] * fo_a) * inv_a);
           out[qh_b * kD + d0] =
               __float2bfloat16_rn((acc[mt][1] * fa_b + mo[(2 * tig + 1) * kD + d0] * fo_b) * inv_b);
           out[qh_a * kD + d0 + 8] =
@@ -368,20 +385,20 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
         __threadfence();
       }
     }
-    named_bar_sync(1, kConsumerWarps * 32);
+    __syncthreads();
     if (nchunks > 1) {
       // ---- the last chunk of the request to finish merges all chunks
       if (tid == 0) {
         const int old = atomicAdd(&a.counters[req], 1);
         *s_flag = old == nchunks - 1;
       }
-      named_bar_sync(1, kConsumerWarps * 32);
+      __syncthreads();
       if (*s_flag) {
         __threadfence();
         const float* pml = a.part_ml + (int64_t)req * a.max_chunks * (kH * 2);
         const float* po = a.part_o + (int64_t)req * a.max_chunks * (kH * kD);
         __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)req * a.out_stride;
-        for (int e = tid; e < kH * kD; e += kConsumerWarps * 32) {
+        for (int e = tid; e < kH * kD; e += kThreadsFast) {
           const int qh = e / kD;
           float M = kNegInf;
           for (int c = 0; c < nchunks; ++c) M = fmaxf(M, __ldcg(pml + c * (kH * 2) + qh * 2));
@@ -395,9 +412,10 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
         }
         if (tid == 0) a.counters[req] = 0;
       }
-      named_bar_sync(1, kConsumerWarps * 32);
+      __syncthreads();
     }
   }
+  cp_async_wait<0>();
 }
 
 // ------------------------------------------------------------------ generic path

@@ -295,7 +295,7 @@ extern "C" int qq_quest_decode_step(const qq_quest_state* st, int flags, int lay
   a.flags = flags;
   a.layer_begin = layer_begin;
   a.nlayers = layer_end - layer_begin;
-  a.groups = std::min(a.nlayers, 8);
+  a.groups = a.nlayers;  // one block per (request, layer): every load of the step in flight at once
   a.row_stride = k_row_stride;
   if (fold)
     for (int l = 0; l < a.nlayers; ++l) a.kp.k[l] = k_layers[l];
@@ -310,8 +310,8 @@ extern "C" int qq_quest_decode_step(const qq_quest_state* st, int flags, int lay
   dim3 grid(batch->bs, a.groups);
   cudaStream_t s = as_stream(stream);
   if (kv_dtype == QQ_F32)
-    decode_step_kernel<float><<<grid, 256, 0, s>>>(a);
+    decode_step_kernel<float><<<grid, 128, 0, s>>>(a);
   else
-    decode_step_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
+    decode_step_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(a);
   return launch_status();
 }

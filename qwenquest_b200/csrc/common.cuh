@@ -133,11 +133,12 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
 
 // ---------------------------------------------------------------- loads
 
+// Read-only streaming 128-bit load (not volatile: the compiler may batch them).
 __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
   uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p));
   return r;
 }
 

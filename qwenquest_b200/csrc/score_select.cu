@@ -127,27 +127,35 @@ __global__ void __launch_bounds__(kThreads) score_select_kernel(SelectArgs a) {
     }
     const uint16_t* breq = st.page_bounds +
                            (((size_t)a.layer * st.max_reqs + req) * st.max_pages) * (size_t)nch * 2;
-    for (int64_t p = p0 + warp; p < p1; p += kWarps) {
-      const uint4* pb = reinterpret_cast<const uint4*>(breq + (size_t)p * nch * 2);
-      uint4 w[KITER];
+    // two pages per warp iteration: 2 * KITER independent 128-bit loads in flight per lane
+    for (int64_t p = p0 + warp; p < p1; p += 2 * kWarps) {
+      const int64_t pp[2] = {p, p + kWarps};
+      uint4 w[2][KITER];
 #pragma unroll
-      for (int it = 0; it < KITER; ++it) {
-        const int j = lane + 32 * it;
-        w[it] = j < nvec ? ld_stream_u4(pb + j) : make_uint4(0, 0, 0, 0);
-      }
-      float acc = 0.f;
+      for (int u = 0; u < 2; ++u) {
+        const uint4* pb = reinterpret_cast<const uint4*>(breq + (size_t)pp[u] * nch * 2);
 #pragma unroll
-      for (int it = 0; it < KITER; ++it) {
-        if (lane + 32 * it < nvec) {
-          acc = __fadd_rn(acc, bound_term(w[it].x, qv[it][0]));
-          acc = __fadd_rn(acc, bound_term(w[it].y, qv[it][1]));
-          acc = __fadd_rn(acc, bound_term(w[it].z, qv[it][2]));
-          acc = __fadd_rn(acc, bound_term(w[it].w, qv[it][3]));
+        for (int it = 0; it < KITER; ++it) {
+          const int j = lane + 32 * it;
+          w[u][it] = (j < nvec && pp[u] < p1) ? ld_stream_u4(pb + j) : make_uint4(0, 0, 0, 0);
         }
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-      if (lane == 0) scores[p] = acc;
+      for (int u = 0; u < 2; ++u) {
+        float acc = 0.f;
+#pragma unroll
+        for (int it = 0; it < KITER; ++it) {
+          if (lane + 32 * it < nvec) {
+            acc = __fadd_rn(acc, bound_term(w[u][it].x, qv[it][0]));
+            acc = __fadd_rn(acc, bound_term(w[u][it].y, qv[it][1]));
+            acc = __fadd_rn(acc, bound_term(w[u][it].z, qv[it][2]));
+            acc = __fadd_rn(acc, bound_term(w[u][it].w, qv[it][3]));
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        if (lane == 0 && pp[u] < p1) scores[pp[u]] = acc;
+      }
     }
   }
   if (a.score_all) return;
