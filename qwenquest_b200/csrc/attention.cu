@@ -44,6 +44,9 @@ constexpr int kThreadsFast = kWarpsFast * 32;
 constexpr int kSlotBytes = 2 * kToks * kPitch;  // K tile + V tile
 constexpr int kMergeFloats = kKV * kG * kD;     // 4096
 constexpr int kCopiesPerThread = kToks * 2 * kRowBytes / 16 / kThreadsFast;  // 16
+// chunks per request the in-kernel merge handles (its staging lives in the
+// 4096-float merge buffer: chunks x 32 heads x 3 floats); top_k <= 32 * 128
+constexpr int kMaxChunksFast = 32;
 constexpr size_t kSmemFast = (size_t)kSlots * kSlotBytes + sizeof(float) * (kMergeFloats + 2 * kKV * kG) + 16;
 
 struct AttnArgs {
@@ -168,18 +171,22 @@ __device__ __forceinline__ bool next_stage(const AttnArgs& a, Cursor& c, int tot
   return false;
 }
 
+// Lane l's pool row for row l of stage `c` (loaded one iteration before use).
+__device__ __forceinline__ int32_t load_stage_row(const AttnArgs& a, const Cursor& c, int lane) {
+  const int ntok = min(kToks, c.cnt - c.sub * kToks);
+  return lane < ntok ? __ldg(a.rows + (int64_t)c.req * a.top_k + c.base + c.sub * kToks + lane) : 0;
+}
+
 // Gather the 32 K and V rows of stage `c` into `slot` (all 256 threads,
 // kCopiesPerThread 16-byte copies each; a warp copies 512 contiguous bytes).
-__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Cursor& c, char* slot, int warp, int lane) {
-  const int r0 = c.base + c.sub * kToks;
+// `row_l` is this lane's value from load_stage_row.
+__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Cursor& c, int32_t row_l, char* slot, int warp,
+                                            int lane) {
   const int ntok = min(kToks, c.cnt - c.sub * kToks);
-  int64_t my_row = 0;  // lane l holds the pool row of stage row l
-  if (lane < ntok) {
-    my_row = __ldg(a.rows + (int64_t)c.req * a.top_k + r0 + lane);
-    if (my_row < 0 || my_row >= a.num_rows) {
-      raise_error(a.err, QQ_DEV_ERR_BOUNDS);
-      my_row = 0;
-    }
+  int64_t my_row = row_l;  // lane l holds the pool row of stage row l
+  if (lane < ntok && (my_row < 0 || my_row >= a.num_rows)) {
+    raise_error(a.err, QQ_DEV_ERR_BOUNDS);
+    my_row = 0;
   }
   const int sub_row = warp >> 2;           // 0/1: which of the two rows this warp copies per round
   const int chunk = (warp & 3) * 32 + lane;  // 16-byte chunk within the 2 KiB (K | V) row
@@ -210,11 +217,18 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
   const int total_items = a.bs * a.max_chunks;
   const __nv_bfloat16* qbase = static_cast<const __nv_bfloat16*>(a.q);
 
-  // prologue: put kSlots - 1 stages in flight
+  // prologue: put kSlots - 1 stages in flight; the fetch cursor's row
+  // indices are always loaded one stage ahead of their use
   Cursor fc{-1, 0, 0, 0, 0}, cc{-1, 0, 0, 0, 0};
+  bool have_f = next_stage(a, fc, total_items);
+  int32_t row_f = have_f ? load_stage_row(a, fc, lane) : 0;
 #pragma unroll
   for (int s = 0; s < kSlots - 1; ++s) {
-    if (next_stage(a, fc, total_items)) issue_stage(a, fc, smem + (size_t)s * kSlotBytes, warp, lane);
+    if (have_f) {
+      issue_stage(a, fc, row_f, smem + (size_t)s * kSlotBytes, warp, lane);
+      have_f = next_stage(a, fc, total_items);
+      if (have_f) row_f = load_stage_row(a, fc, lane);
+    }
     cp_async_commit();
   }
 
@@ -225,8 +239,11 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
   while (next_stage(a, cc, total_items)) {
     cp_async_wait<kSlots - 2>();
     __syncthreads();  // stage g visible to all; slot (g - 1) % kSlots free
-    if (next_stage(a, fc, total_items))
-      issue_stage(a, fc, smem + (size_t)((g + kSlots - 1) % kSlots) * kSlotBytes, warp, lane);
+    if (have_f) {
+      issue_stage(a, fc, row_f, smem + (size_t)((g + kSlots - 1) % kSlots) * kSlotBytes, warp, lane);
+      have_f = next_stage(a, fc, total_items);
+      if (have_f) row_f = load_stage_row(a, fc, lane);
+    }
     cp_async_commit();
 
     if (cc.sub == 0) {
@@ -394,21 +411,51 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_fast_kernel(AttnArgs a) 
       }
       __syncthreads();
       if (*s_flag) {
+        // merge the request's chunks: (m, l) of every (chunk, head) staged in
+        // shared memory with one batch of loads, per-head weights computed
+        // once, then each thread combines 16 outputs with independent float4 loads
         __threadfence();
         const float* pml = a.part_ml + (int64_t)req * a.max_chunks * (kH * 2);
         const float* po = a.part_o + (int64_t)req * a.max_chunks * (kH * kD);
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)req * a.out_stride;
-        for (int e = tid; e < kH * kD; e += kThreadsFast) {
-          const int qh = e / kD;
+        float* s_pml = s_merge;                      // [nchunks][kH][2]
+        float* s_w = s_merge + kMaxChunksFast * kH * 2;  // [nchunks][kH]
+        for (int t = tid; t < nchunks * kH * 2; t += kThreadsFast) s_pml[t] = __ldcg(pml + t);
+        __syncthreads();
+        if (tid < kH) {
           float M = kNegInf;
-          for (int c = 0; c < nchunks; ++c) M = fmaxf(M, __ldcg(pml + c * (kH * 2) + qh * 2));
-          float S = 0.f, O = 0.f;
-          for (int c = 0; c < nchunks; ++c) {
-            const float f = fast_exp2(__ldcg(pml + c * (kH * 2) + qh * 2) - M);
-            S += __ldcg(pml + c * (kH * 2) + qh * 2 + 1) * f;
-            O += __ldcg(po + c * (kH * kD) + e) * f;
+          for (int c = 0; c < nchunks; ++c) M = fmaxf(M, s_pml[(c * kH + tid) * 2]);
+          float S = 0.f;
+          for (int c = 0; c < nchunks; ++c) S += s_pml[(c * kH + tid) * 2 + 1] * fast_exp2(s_pml[(c * kH + tid) * 2] - M);
+          const float inv = 1.f / S;
+          for (int c = 0; c < nchunks; ++c) s_w[c * kH + tid] = fast_exp2(s_pml[(c * kH + tid) * 2] - M) * inv;
+        }
+        __syncthreads();
+        constexpr int kPer = kH * kD / kThreadsFast;  // 16 consecutive outputs per thread
+        const int e0 = tid * kPer;
+        const int qh = e0 / kD;
+        float o[kPer];
+#pragma unroll
+        for (int v = 0; v < kPer; ++v) o[v] = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < nchunks; ++c) {
+          const float w = s_w[c * kH + qh];
+          const float4* src = reinterpret_cast<const float4*>(po + (int64_t)c * (kH * kD) + e0);
+#pragma unroll
+          for (int v = 0; v < kPer / 4; ++v) {
+            const float4 x = __ldcg(src + v);
+            o[4 * v] += w * x.x;
+            o[4 * v + 1] += w * x.y;
+            o[4 * v + 2] += w * x.z;
+            o[4 * v + 3] += w * x.w;
           }
-          out[e] = __float2bfloat16_rn(O / S);
+        }
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)req * a.out_stride + e0;
+#pragma unroll
+        for (int v = 0; v < kPer; v += 2) {
+          __nv_bfloat162 pair;
+          pair.x = __float2bfloat16_rn(o[v]);
+          pair.y = __float2bfloat16_rn(o[v + 1]);
+          *reinterpret_cast<__nv_bfloat162*>(out + v) = pair;
         }
         if (tid == 0) a.counters[req] = 0;
       }
@@ -542,7 +589,8 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
 
   const bool fast = dtype == QQ_BF16 && kv_heads == kKV && head_dim == kD && q_heads == kH &&
                     kv_row_stride == kKV * kD && (reinterpret_cast<uintptr_t>(k_pool) % 16) == 0 &&
-                    (reinterpret_cast<uintptr_t>(v_pool) % 16) == 0 && (q_stride % 2) == 0;
+                    (reinterpret_cast<uintptr_t>(v_pool) % 16) == 0 && (q_stride % 2) == 0 &&
+                    (out_stride % 2) == 0 && a.max_chunks <= kMaxChunksFast;
   if (fast) {
     static bool attr_set = false;
     if (!attr_set) {
