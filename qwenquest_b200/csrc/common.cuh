@@ -159,7 +159,7 @@ inline int32_t* ws_counters(void* ws, CounterSlot slot) {
   return reinterpret_cast<int32_t*>(static_cast<char*>(ws) + slot * kCounterBytes);
 }
 constexpr size_t kPartialOffset = 3 * kCounterBytes;
-constexpr int kAttnChunk = 128;  // rows per split of the attention kernel
+constexpr int kAttnChunk = 64;  // rows per split (work unit) of the attention kernel
 
 inline size_t attn_partial_floats(int bs, int top_k, int q_heads, int head_dim) {
   const size_t chunks = (size_t)((top_k + kAttnChunk - 1) / kAttnChunk);
