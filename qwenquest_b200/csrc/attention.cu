@@ -1,27 +1,29 @@
 // [Q7] Split-K sparse decode attention over an explicit row list.
 //
-// Fast path (bf16, 4 KV heads, head_dim 128, 8 query heads per KV head),
-// two launches:
+// Fast path (bf16, 4 KV heads, head_dim 128, 8 query heads per KV head):
+// one launch, one 256-thread block per SM, every warp an independent
+// pipeline over a stream-K split of the work.
 //
-// 1. attn_stream_kernel — one 256-thread block per SM, and every warp is an
-//    independent pipeline.  Work unit = (request, KV head, chunk of 64 rows
-//    of the request's row list); units go round-robin to the warps of the
-//    grid, so the four warps of a block that share a chunk read the four
-//    256-byte head slices of the same rows.  A warp gathers only its own
-//    head's K and V slices: per 16-row stage each lane issues 16 16-byte
-//    cp.async.cg copies (one instruction = 256 B of K + 256 B of V of a row),
-//    into a private 3-slot ring at a 272-byte row pitch (ldmatrix reads are
-//    bank-conflict free), with an L2 evict-first policy (every K/V byte is
-//    read once).  Waits are per warp (cp.async.wait_group + __syncwarp): no
-//    block barrier, atomic or fence in the streaming loop, so one warp's slow
-//    request never stalls the others.  Per stage:
-//      S^T[16 rows x 8 heads] = K[16 x 128] . Q^T[128 x 8]   (8 x mma m16n8k16)
-//      online softmax in fp32 (exp2 domain), P^T via movmatrix.trans
-//      O^T[128 x 8] += V^T[128 x 16] . P^T[16 x 8]          (P as bf16 hi + lo: 16 mma)
-//    At the end of a unit the warp writes its fp32 partial (m, l, O) to the
-//    workspace.
-// 2. attn_merge_kernel — block (request, KV head) combines the partials of
-//    the request's chunks into the bf16 output.
+// * Work space: the (request, KV head) segments in order, segment (i, h)
+//   holding the n_i = min(seq_len_i, top_k) rows of request i; each warp of
+//   the grid takes one contiguous, equal share of the flattened rows.  A
+//   segment that lies inside one warp's share is finished by that warp and
+//   written straight to the output; only the first and last segment of a
+//   share can be split, so a warp writes at most two fp32 partials
+//   (m, l, O), and the last warp to finish a split segment (an arrival
+//   counter in the workspace) merges it.
+// * Data movement: a warp gathers only its own KV head's 256-byte K and V
+//   slices.  Per 16-row stage each lane issues 16 cp.async.cg copies of 16
+//   bytes (one instruction = 256 B of K + 256 B of V of a row) into a private
+//   3-slot ring at a 272-byte row pitch (ldmatrix reads are bank-conflict
+//   free).  A look-ahead cursor prefetches the rows of the stage three
+//   stages beyond the newest copy into L2, so ~6 stages per warp are in
+//   flight while only 3 occupy shared memory.  Waits are per warp
+//   (cp.async.wait_group + __syncwarp): no block barrier in the loop.
+// * Math per stage:
+//     S^T[16 rows x 8 heads] = K[16 x 128] . Q^T[128 x 8]   (8 x mma m16n8k16)
+//     online softmax in fp32 (exp2 domain), P^T via movmatrix.trans
+//     O^T[128 x 8] += V^T[128 x 16] . P^T[16 x 8]          (P as bf16 hi + lo: 16 mma)
 //
 // Generic path (any head_dim / group / fp32): one block per (request, KV
 // head), scores in shared memory, two-pass softmax, fp32 FMA.
@@ -41,21 +43,21 @@ constexpr int kH = kKV * kG;
 constexpr int kSlice = kD * 2;          // 256 bytes: one KV head of one row
 constexpr int kPitch = kSlice + 16;     // 272
 constexpr int kToks = 16;               // rows per stage (the MMA's M)
-constexpr int kSlots = 3;               // stages in a warp's ring
-constexpr int kUnitRows = kAttnChunk;   // 64 rows per work unit
-constexpr int kWarpsFast = 8;
+constexpr int kSlots = 3;               // stages in a warp's shared-memory ring
+constexpr int kLookahead = 3;           // L2 prefetch distance beyond the newest copy, in stages
+constexpr int kMinShare = 64;           // rows per warp at least
+constexpr int kWarpsFast = kAttnWarpsPerSm;
 constexpr int kThreadsFast = kWarpsFast * 32;
 constexpr int kSlotBytes = 2 * kToks * kPitch;  // K slice tile + V slice tile: 8704
 constexpr int kWarpSmem = kSlots * kSlotBytes;  // 26112
-constexpr size_t kSmemFast = (size_t)kWarpsFast * kWarpSmem;  // 208896
-constexpr int kMaxChunksFast = 64;      // top_k <= 4096 on the fast path
-constexpr int kMergeThreads = 256;
+constexpr size_t kSmemRing = (size_t)kWarpsFast * kWarpSmem;            // 208896
+constexpr size_t kSmemFast = kSmemRing + sizeof(int32_t) * (QQ_MAX_BS + 1);  // + segment prefix
+constexpr int kPartFloats = kG * kD + 2 * kG;   // one partial record: O [8][128], (m, l) [8]
 
 struct AttnArgs {
   const int64_t* seq_lens;
   int bs;
   int top_k;
-  int max_chunks;  // 64-row chunks per request at top_k
   const void* q;
   int64_t q_stride;
   const int32_t* rows;
@@ -68,9 +70,8 @@ struct AttnArgs {
   void* out;
   int64_t out_stride;
   uint32_t* err;
-  float* part_o;   // [bs][max_chunks][kKV][kG][kD]
-  float* part_ml;  // [bs][max_chunks][kKV][kG][2]
-  int32_t* counters;
+  float* part;        // [warps][2][kPartFloats]
+  int32_t* seg_count; // [bs * kKV] arrival counters of split segments
 };
 
 __device__ __forceinline__ void ldmatrix_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
@@ -117,17 +118,10 @@ __device__ __forceinline__ uint32_t pack_bf16x2_split(float lo, float hi, float&
 
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
-__device__ __forceinline__ uint64_t evict_first_policy() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-
-// 16-byte async copy global -> shared with an L2 cache policy; src_bytes = 0 writes zeros.
-__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src, uint32_t src_bytes,
-                                            uint64_t policy) {
-  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(smem_u32(smem_dst)),
-               "l"(gmem_src), "r"(src_bytes), "l"(policy)
+// 16-byte async copy global -> shared; src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
+               "r"(src_bytes)
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -136,96 +130,189 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 #define kNegInf (-__int_as_float(0x7f800000))
 
-// A position in a warp's stream of stages: stage `sub` of work unit `unit`.
-struct Cursor {
-  int unit;  // -1 before the first stage, >= total when exhausted
-  int sub;
-  int cnt;   // rows of the unit
-  int req;   // batch index
-  int head;  // KV head
-  int chunk; // 64-row chunk of the request's row list
+// ------------------------------------------------------------------ stream-K walk
+//
+// Flattened position p in [0, T), T = 4 * sum_i n_i: segment (i, h) covers
+// [4 P_i + h n_i, 4 P_i + (h + 1) n_i) with P_i = sum_{j<i} n_j.  Warp w of
+// NW owns [B(w), B(w + 1)), B(w) = floor(w T / NW).
+
+struct Split {
+  const int32_t* prefix4;  // shared: 4 * P_i, i = 0..bs
+  int bs;
+  int64_t T;
+  int NW;
+  __device__ __forceinline__ int64_t begin(int w) const { return (int64_t)w * T / NW; }
+  // warp owning position p
+  __device__ __forceinline__ int owner(int64_t p) const { return (int)(((p + 1) * NW - 1) / T); }
 };
 
-// Advance to the next stage of the warp's stream (units W, W + NW, ...).
-__device__ __forceinline__ bool next_stage(const AttnArgs& a, Cursor& c, int W, int NW, int total_units) {
-  if (c.unit >= 0 && c.unit < total_units && (c.sub + 1) * kToks < c.cnt) {
-    ++c.sub;
-    return true;
+struct Walk {
+  int64_t begin;           // start of the share
+  int64_t pos, end;        // next position to issue, end of the share
+  int req, head, n;        // current segment
+  int64_t seg_start;
+  // the stage last produced by next():
+  int r0, cnt;             // rows [r0, r0 + cnt) of segment (req, head)
+  int64_t stage_seg_start;
+  int s_req, s_head, s_n;
+  bool s_first, s_last;    // stage opens / closes this warp's portion of the segment
+};
+
+__device__ __forceinline__ void walk_seek(const Split& sp, Walk& w, int64_t p) {
+  // segment containing p: largest i with prefix4[i] <= p, then the head
+  int lo = 0, hi = sp.bs;  // prefix4[lo] <= p < prefix4[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (sp.prefix4[mid] <= p) lo = mid; else hi = mid;
   }
-  for (int u = c.unit < 0 ? W : c.unit + NW; u < total_units; u += NW) {
-    const int head = u & (kKV - 1);
-    const int rest = u >> 2;
-    const int req = rest / a.max_chunks;
-    const int chunk = rest - req * a.max_chunks;
-    const int64_t L = __ldg(a.seq_lens + req);
-    const int n = (int)(L < a.top_k ? L : a.top_k);
-    const int cnt = min(kUnitRows, n - chunk * kUnitRows);
-    if (cnt > 0) {
-      c.unit = u;
-      c.sub = 0;
-      c.cnt = cnt;
-      c.req = req;
-      c.head = head;
-      c.chunk = chunk;
-      return true;
+  w.req = lo;
+  w.n = (sp.prefix4[lo + 1] - sp.prefix4[lo]) >> 2;
+  w.head = (int)((p - sp.prefix4[lo]) / w.n);
+  w.seg_start = sp.prefix4[lo] + (int64_t)w.head * w.n;
+}
+
+__device__ __forceinline__ void walk_init(const Split& sp, Walk& w, int warp_id) {
+  w.begin = w.pos = sp.begin(warp_id);
+  w.end = sp.begin(warp_id + 1);
+  if (w.pos < w.end) walk_seek(sp, w, w.pos);
+}
+
+__device__ __forceinline__ bool walk_next(const Split& sp, Walk& w) {
+  if (w.pos >= w.end) return false;
+  const int64_t seg_end = w.seg_start + w.n;
+  const int64_t stop = min(min(w.pos + kToks, seg_end), w.end);
+  w.r0 = (int)(w.pos - w.seg_start);
+  w.cnt = (int)(stop - w.pos);
+  w.stage_seg_start = w.seg_start;
+  w.s_req = w.req;
+  w.s_head = w.head;
+  w.s_n = w.n;
+  w.s_first = w.r0 == 0 || w.pos == w.begin;
+  w.s_last = stop == seg_end || stop == w.end;
+  w.pos = stop;
+  if (stop == seg_end && stop < w.end) {
+    if (++w.head == kKV) {
+      w.head = 0;
+      ++w.req;
+      // skip empty requests (seq_len 0 cannot occur in decode, kept for safety)
+      while (w.req < sp.bs && sp.prefix4[w.req + 1] == sp.prefix4[w.req]) ++w.req;
+      w.n = (sp.prefix4[w.req + 1] - sp.prefix4[w.req]) >> 2;
+      w.seg_start = sp.prefix4[w.req];
+    } else {
+      w.seg_start += w.n;
     }
   }
-  c.unit = total_units;
-  return false;
+  return true;
 }
 
-// Lane l's pool row for row l of stage `c` (lanes >= 16 and rows past the end: 0).
-__device__ __forceinline__ int32_t load_stage_row(const AttnArgs& a, const Cursor& c, int lane) {
-  const int ntok = min(kToks, c.cnt - c.sub * kToks);
-  return lane < ntok
-             ? __ldg(a.rows + (int64_t)c.req * a.top_k + c.chunk * kUnitRows + c.sub * kToks + lane)
-             : 0;
+// Lane l's pool row for row l of the walk's current stage (lanes >= cnt: 0).
+__device__ __forceinline__ int32_t stage_row(const AttnArgs& a, const Walk& w, int lane) {
+  return lane < w.cnt ? __ldg(a.rows + (int64_t)w.s_req * a.top_k + w.r0 + lane) : 0;
 }
 
-// Gather the head slices of the stage's 16 K and V rows into `slot`: per row
-// one warp instruction, lanes 0-15 K bytes [16 l, 16 l + 16), lanes 16-31 V.
-__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Cursor& c, int32_t row_l, char* slot, int lane,
-                                            uint64_t policy) {
-  const int ntok = min(kToks, c.cnt - c.sub * kToks);
-  int64_t my_row = row_l;
-  if (lane < ntok && (my_row < 0 || my_row >= a.num_rows)) {
+__device__ __forceinline__ int64_t checked_row(const AttnArgs& a, int32_t row, bool valid) {
+  if (valid && (row < 0 || row >= a.num_rows)) {
     raise_error(a.err, QQ_DEV_ERR_BOUNDS);
-    my_row = 0;
+    return 0;
   }
+  return valid ? row : 0;
+}
+
+// Gather the head slices of the stage's rows into `slot`: per row one warp
+// instruction, lanes 0-15 K bytes [16 l, 16 l + 16), lanes 16-31 V.
+__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, int32_t row_l, char* slot, int lane) {
+  const int64_t my_row = checked_row(a, row_l, lane < w.cnt);
   const bool is_v = lane >= 16;
   const int off = (lane & 15) * 16;
-  const char* src0 = (is_v ? a.v_pool : a.k_pool) + c.head * kSlice + off;
+  const char* src0 = (is_v ? a.v_pool : a.k_pool) + w.s_head * kSlice + off;
   char* dst0 = slot + (is_v ? kToks * kPitch : 0) + off;
 #pragma unroll
   for (int k = 0; k < kToks; ++k) {
     const int64_t row = __shfl_sync(0xffffffffu, my_row, k);
-    cp_async_16(dst0 + k * kPitch, src0 + row * a.row_stride_bytes, k < ntok ? 16u : 0u, policy);
+    cp_async_16(dst0 + k * kPitch, src0 + row * a.row_stride_bytes, k < w.cnt ? 16u : 0u);
+  }
+}
+
+// L2 prefetch of the head slices of a stage's rows (two 128-byte lines of K and of V per row).
+__device__ __forceinline__ void prefetch_stage(const AttnArgs& a, const Walk& w, int32_t row_l, int lane) {
+  if (lane < w.cnt) {
+    const int64_t row = checked_row(a, row_l, true);
+    const char* kp = a.k_pool + row * a.row_stride_bytes + w.s_head * kSlice;
+    const char* vp = a.v_pool + row * a.row_stride_bytes + w.s_head * kSlice;
+    prefetch_l2(kp);
+    prefetch_l2(kp + 128);
+    prefetch_l2(vp);
+    prefetch_l2(vp + 128);
   }
 }
 
 __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a) {
   extern __shared__ __align__(128) char smem[];
+  int32_t* s_prefix4 = reinterpret_cast<int32_t*>(smem + kSmemRing);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  char* ring = smem + (size_t)warp * kWarpSmem;
+
+  // segment prefix 4 * P_i over the batch (warp 0, 32 requests at a time)
+  if (warp == 0) {
+    int32_t run = 0;
+    for (int b0 = 0; b0 < a.bs; b0 += 32) {
+      const int b = b0 + lane;
+      int32_t n = 0;
+      if (b < a.bs) {
+        const int64_t L = a.seq_lens[b];
+        n = (int32_t)(L < a.top_k ? (L < 0 ? 0 : L) : a.top_k);
+      }
+      int32_t incl = 4 * n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (b < a.bs) s_prefix4[b + 1] = run + incl;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) s_prefix4[0] = 0;
+  }
+  __syncthreads();
+
+  Split sp;
+  sp.prefix4 = s_prefix4;
+  sp.bs = a.bs;
+  sp.T = s_prefix4[a.bs];
+  if (sp.T == 0) return;
+  const int grid_warps = gridDim.x * kWarpsFast;
+  sp.NW = (int)min((int64_t)grid_warps, max((int64_t)1, sp.T / kMinShare));
   const int W = blockIdx.x * kWarpsFast + warp;
-  const int NW = gridDim.x * kWarpsFast;
-  const int total_units = a.bs * a.max_chunks * kKV;
-  const uint64_t policy = evict_first_policy();
+  if (W >= sp.NW) return;
+
+  char* ring = smem + (size_t)warp * kWarpSmem;
   const __nv_bfloat16* qbase = static_cast<const __nv_bfloat16*>(a.q);
 
-  // prologue: kSlots - 1 stages in flight; row indices always one stage ahead
-  Cursor fc{-1, 0, 0, 0, 0, 0}, cc{-1, 0, 0, 0, 0, 0};
-  bool have_f = next_stage(a, fc, W, NW, total_units);
-  int32_t row_f = have_f ? load_stage_row(a, fc, lane) : 0;
+  // cursors: pc prefetches into L2, fc copies into the ring, cc computes
+  Walk pc, fc, cc;
+  walk_init(sp, pc, W);
+  fc = pc;
+  cc = pc;
+  const int64_t share_begin = pc.pos;
+  bool have_p = walk_next(sp, pc);
+  int32_t row_p = have_p ? stage_row(a, pc, lane) : 0;
+  for (int s = 0; s < kSlots - 1 + kLookahead && have_p; ++s) {
+    prefetch_stage(a, pc, row_p, lane);
+    have_p = walk_next(sp, pc);
+    row_p = have_p ? stage_row(a, pc, lane) : 0;
+  }
+  bool have_f = walk_next(sp, fc);
 #pragma unroll
   for (int s = 0; s < kSlots - 1; ++s) {
     if (have_f) {
-      issue_stage(a, fc, row_f, ring + s * kSlotBytes, lane, policy);
-      have_f = next_stage(a, fc, W, NW, total_units);
-      if (have_f) row_f = load_stage_row(a, fc, lane);
+      issue_stage(a, fc, stage_row(a, fc, lane), ring + s * kSlotBytes, lane);
+      have_f = walk_next(sp, fc);
     }
     cp_async_commit();
   }
@@ -234,12 +321,12 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a
   float acc[8][4];
   float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
   int g = 0;
-  while (next_stage(a, cc, W, NW, total_units)) {
-    if (cc.sub == 0) {
-      // Q^T fragments of this KV head: B[k = d][n = query head]; loaded before
-      // the wait so their latency hides behind it
-      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qbase + (int64_t)cc.req * a.q_stride +
-                                                               (int64_t)(cc.head * kG + gid) * kD);
+  while (walk_next(sp, cc)) {
+    if (cc.s_first) {
+      // a new portion of a segment: Q^T fragments of this KV head, loaded
+      // before the wait so their latency hides behind it
+      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qbase + (int64_t)cc.s_req * a.q_stride +
+                                                               (int64_t)(cc.s_head * kG + gid) * kD);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         qb[kk][0] = __ldg(qrow + (kk * 16 + 2 * tig) / 2);
@@ -251,15 +338,19 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a
       l_a = l_b = 0.f;
     }
     cp_async_wait<kSlots - 2>();
-    __syncwarp();  // stage g visible to every lane; slot of stage g - 1 free
+    __syncwarp();  // stage g visible to every lane; the slot of stage g - 1 is free
     if (have_f) {
-      issue_stage(a, fc, row_f, ring + ((g + kSlots - 1) % kSlots) * kSlotBytes, lane, policy);
-      have_f = next_stage(a, fc, W, NW, total_units);
-      if (have_f) row_f = load_stage_row(a, fc, lane);
+      issue_stage(a, fc, stage_row(a, fc, lane), ring + ((g + kSlots - 1) % kSlots) * kSlotBytes, lane);
+      have_f = walk_next(sp, fc);
     }
     cp_async_commit();
+    if (have_p) {
+      prefetch_stage(a, pc, row_p, lane);
+      have_p = walk_next(sp, pc);
+      row_p = have_p ? stage_row(a, pc, lane) : 0;
+    }
 
-    const int ntok = min(kToks, cc.cnt - cc.sub * kToks);
+    const int ntok = cc.cnt;
     const char* sk = ring + (g % kSlots) * kSlotBytes;
     const char* sv = sk + kToks * kPitch;
     // ---- S^T = K . Q^T
@@ -319,78 +410,102 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a
       mma_bf16_16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
     }
     ++g;
-    if ((cc.sub + 1) * kToks < cc.cnt) continue;
+    if (!cc.s_last) continue;
 
-    // ---- end of the unit: fp32 partial (m, l, O) of (request, chunk, KV head)
+    // ---- end of this warp's portion of segment (req, head)
     float la = l_a, lb = l_b;
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       la += __shfl_xor_sync(0xffffffffu, la, o);
       lb += __shfl_xor_sync(0xffffffffu, lb, o);
     }
-    const int64_t pu = ((int64_t)cc.req * a.max_chunks + cc.chunk) * kKV + cc.head;
-    float* po = a.part_o + pu * (kG * kD);
+    const int64_t seg0 = cc.stage_seg_start;
+    const int64_t seg1 = seg0 + cc.s_n;
+    const int w_first = sp.owner(seg0), w_last = sp.owner(seg1 - 1);
+    const int qh_a = cc.s_head * kG + 2 * tig, qh_b = qh_a + 1;  // this thread's query heads
+    if (w_first == w_last) {
+      // the whole segment is this warp's: normalize and write bf16
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)cc.s_req * a.out_stride;
+      const float inv_a = 1.f / la, inv_b = 1.f / lb;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int d0 = mt * 16 + gid;
+        out[qh_a * kD + d0] = __float2bfloat16_rn(acc[mt][0] * inv_a);
+        out[qh_b * kD + d0] = __float2bfloat16_rn(acc[mt][1] * inv_b);
+        out[qh_a * kD + d0 + 8] = __float2bfloat16_rn(acc[mt][2] * inv_a);
+        out[qh_b * kD + d0 + 8] = __float2bfloat16_rn(acc[mt][3] * inv_b);
+      }
+      continue;
+    }
+    // split segment: record (m, l, O) in slot 0 (the share's first segment) or 1
+    const int slot = seg0 <= share_begin ? 0 : 1;
+    float* rec = a.part + ((int64_t)W * 2 + slot) * kPartFloats;
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
       const int d0 = mt * 16 + gid;
-      po[(2 * tig) * kD + d0] = acc[mt][0];
-      po[(2 * tig + 1) * kD + d0] = acc[mt][1];
-      po[(2 * tig) * kD + d0 + 8] = acc[mt][2];
-      po[(2 * tig + 1) * kD + d0 + 8] = acc[mt][3];
+      rec[(2 * tig) * kD + d0] = acc[mt][0];
+      rec[(2 * tig + 1) * kD + d0] = acc[mt][1];
+      rec[(2 * tig) * kD + d0 + 8] = acc[mt][2];
+      rec[(2 * tig + 1) * kD + d0 + 8] = acc[mt][3];
     }
     if (gid == 0) {
-      float* pml = a.part_ml + pu * (kG * 2);
-      pml[(2 * tig) * 2] = m_a;
-      pml[(2 * tig) * 2 + 1] = la;
-      pml[(2 * tig + 1) * 2] = m_b;
-      pml[(2 * tig + 1) * 2 + 1] = lb;
+      float* ml = rec + kG * kD;
+      ml[(2 * tig) * 2] = m_a;
+      ml[(2 * tig) * 2 + 1] = la;
+      ml[(2 * tig + 1) * 2] = m_b;
+      ml[(2 * tig + 1) * 2 + 1] = lb;
+    }
+    __threadfence();
+    __syncwarp();
+    const int seg_id = cc.s_req * kKV + cc.s_head;
+    int old = 0;
+    if (lane == 0) old = atomicAdd(&a.seg_count[seg_id], 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != w_last - w_first) continue;
+
+    // the last warp of the segment merges its records: lane -> head lane / 4,
+    // channels [32 (lane % 4), 32 (lane % 4) + 32)
+    __threadfence();
+    if (lane == 0) a.seg_count[seg_id] = 0;
+    const int hq = lane >> 2, c0 = (lane & 3) * 32;
+    float M = kNegInf;
+    for (int w = w_first; w <= w_last; ++w) {
+      const int sl = (w == w_first && sp.begin(w_first) != seg0) ? 1 : 0;
+      const float* r2 = a.part + ((int64_t)w * 2 + sl) * kPartFloats + kG * kD;
+      M = fmaxf(M, __ldcg(r2 + hq * 2));
+    }
+    float S = 0.f;
+    float o[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) o[e] = 0.f;
+    for (int w = w_first; w <= w_last; ++w) {
+      const int sl = (w == w_first && sp.begin(w_first) != seg0) ? 1 : 0;
+      const float* r2 = a.part + ((int64_t)w * 2 + sl) * kPartFloats;
+      const float mw = __ldcg(r2 + kG * kD + hq * 2);
+      const float f = mw == kNegInf ? 0.f : fast_exp2(mw - M);
+      S += __ldcg(r2 + kG * kD + hq * 2 + 1) * f;
+      const float4* src = reinterpret_cast<const float4*>(r2 + hq * kD + c0);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const float4 x = __ldcg(src + v);
+        o[4 * v] += f * x.x;
+        o[4 * v + 1] += f * x.y;
+        o[4 * v + 2] += f * x.z;
+        o[4 * v + 3] += f * x.w;
+      }
+    }
+    const float inv = 1.f / S;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)cc.s_req * a.out_stride +
+                         (cc.s_head * kG + hq) * kD + c0;
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+      __nv_bfloat162 pr;
+      pr.x = __float2bfloat16_rn(o[e] * inv);
+      pr.y = __float2bfloat16_rn(o[e + 1] * inv);
+      *reinterpret_cast<__nv_bfloat162*>(out + e) = pr;
     }
   }
   cp_async_wait<0>();
-}
-
-// Block (request, KV head): out = sum_c w_c O_c with w_c = 2^(m_c - M) / sum_c l_c 2^(m_c - M).
-__global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnArgs a) {
-  __shared__ float s_w[kMaxChunksFast][kG];
-  const int req = blockIdx.x, head = blockIdx.y, tid = threadIdx.x;
-  const int64_t L = a.seq_lens[req];
-  const int n = (int)(L < a.top_k ? L : a.top_k);
-  const int nch = (n + kUnitRows - 1) / kUnitRows;
-  const int64_t base = (int64_t)req * a.max_chunks * kKV + head;  // unit index of chunk 0
-  if (tid < kG) {
-    float M = kNegInf;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, a.part_ml[(base + (int64_t)c * kKV) * (kG * 2) + tid * 2]);
-    float S = 0.f;
-    for (int c = 0; c < nch; ++c) {
-      const float* ml = a.part_ml + (base + (int64_t)c * kKV) * (kG * 2) + tid * 2;
-      S += ml[1] * fast_exp2(ml[0] - M);
-    }
-    const float inv = 1.f / S;
-    for (int c = 0; c < nch; ++c)
-      s_w[c][tid] = fast_exp2(a.part_ml[(base + (int64_t)c * kKV) * (kG * 2) + tid * 2] - M) * inv;
-  }
-  __syncthreads();
-  constexpr int kPer = kG * kD / kMergeThreads;  // 4 consecutive outputs per thread
-  const int e0 = tid * kPer;
-  const int g = e0 / kD;
-  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-  for (int c = 0; c < nch; ++c) {
-    const float w = s_w[c][g];
-    const float4 x = *reinterpret_cast<const float4*>(a.part_o + (base + (int64_t)c * kKV) * (kG * kD) + e0);
-    o.x += w * x.x;
-    o.y += w * x.y;
-    o.z += w * x.z;
-    o.w += w * x.w;
-  }
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)req * a.out_stride + head * (kG * kD) + e0;
-  __nv_bfloat162 p0, p1;
-  p0.x = __float2bfloat16_rn(o.x);
-  p0.y = __float2bfloat16_rn(o.y);
-  p1.x = __float2bfloat16_rn(o.z);
-  p1.y = __float2bfloat16_rn(o.w);
-  reinterpret_cast<__nv_bfloat162*>(out)[0] = p0;
-  reinterpret_cast<__nv_bfloat162*>(out)[1] = p1;
 }
 
 // ------------------------------------------------------------------ generic path
@@ -473,7 +588,7 @@ using namespace qq;
 
 extern "C" size_t qq_workspace_bytes(int max_bs, int top_k, int q_heads, int head_dim) {
   if (max_bs < 0 || top_k < 0 || q_heads < 0 || head_dim < 0) return 0;
-  return kPartialOffset + sizeof(float) * attn_partial_floats(max_bs, top_k, q_heads, head_dim) + 256;
+  return kPartialOffset + sizeof(float) * attn_partial_floats(sm_count()) + 256;
 }
 
 extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, int dtype,
@@ -496,7 +611,6 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
   a.seq_lens = batch->seq_lens;
   a.bs = batch->bs;
   a.top_k = top_k;
-  a.max_chunks = (top_k + kAttnChunk - 1) / kAttnChunk;
   a.q = q;
   a.q_stride = q_stride;
   a.rows = rows;
@@ -509,17 +623,15 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
   a.out = out;
   a.out_stride = out_stride;
   a.err = err;
-  char* ws = static_cast<char*>(workspace);
-  a.part_o = reinterpret_cast<float*>(ws + kPartialOffset);
-  a.part_ml = a.part_o + (size_t)batch->bs * a.max_chunks * q_heads * head_dim;
-  a.counters = ws_counters(workspace, kCounterAttn);
+  a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kPartialOffset);
+  a.seg_count = ws_counters(workspace, kCounterAttn);
   cudaStream_t s = as_stream(stream);
 
   const bool fast = dtype == QQ_BF16 && kv_heads == kKV && head_dim == kD && q_heads == kH &&
                     (kv_row_stride * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(k_pool) % 16) == 0 &&
                     (reinterpret_cast<uintptr_t>(v_pool) % 16) == 0 && (q_stride % 2) == 0 &&
-                    (out_stride % 4) == 0 && (reinterpret_cast<uintptr_t>(out) % 8) == 0 &&
-                    a.max_chunks <= kMaxChunksFast;
+                    (out_stride % 2) == 0 && (reinterpret_cast<uintptr_t>(out) % 4) == 0 &&
+                    (int64_t)batch->bs * top_k * kKV < (1ll << 31);
   if (fast) {
     static bool attr_set = false;
     if (!attr_set) {
@@ -528,12 +640,7 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
         return QQ_ERR_CUDA;
       attr_set = true;
     }
-    const int units = batch->bs * a.max_chunks * kKV;
-    const int grid = std::max(1, std::min((units + kWarpsFast - 1) / kWarpsFast, sm_count()));
-    attn_stream_kernel<<<grid, kThreadsFast, kSmemFast, s>>>(a);
-    const int rc = launch_status();
-    if (rc != QQ_OK) return rc;
-    attn_merge_kernel<<<dim3(batch->bs, kKV), kMergeThreads, 0, s>>>(a);
+    attn_stream_kernel<<<sm_count(), kThreadsFast, kSmemFast, s>>>(a);
     return launch_status();
   }
   const int G = q_heads / kv_heads;

@@ -151,19 +151,22 @@ inline int launch_status() {
   return e == cudaSuccess ? QQ_OK : QQ_ERR_CUDA;
 }
 
-// Workspace layout: three counter arrays of QQ_MAX_BS int32 (kept at zero
-// between launches), then the attention partials.
+// Workspace layout: arrival counters (int32, kept at zero between launches) —
+// QQ_MAX_BS for the selection, QQ_MAX_BS for the bounds step, 4 * QQ_MAX_BS
+// for the attention's (request, KV head) segments — then the attention partials.
 constexpr size_t kCounterBytes = sizeof(int32_t) * QQ_MAX_BS;
-enum CounterSlot { kCounterSelect = 0, kCounterAttn = 1, kCounterStep = 2 };
+enum CounterSlot { kCounterSelect = 0, kCounterStep = 1, kCounterAttn = 2 };
 inline int32_t* ws_counters(void* ws, CounterSlot slot) {
   return reinterpret_cast<int32_t*>(static_cast<char*>(ws) + slot * kCounterBytes);
 }
-constexpr size_t kPartialOffset = 3 * kCounterBytes;
-constexpr int kAttnChunk = 64;  // rows per split (work unit) of the attention kernel
+constexpr size_t kPartialOffset = 6 * kCounterBytes;
 
-inline size_t attn_partial_floats(int bs, int top_k, int q_heads, int head_dim) {
-  const size_t chunks = (size_t)((top_k + kAttnChunk - 1) / kAttnChunk);
-  return (size_t)bs * chunks * (size_t)q_heads * (size_t)(head_dim + 2);
+// Attention partials: two (m, l, O) records of 8 query heads x 128 channels
+// per warp of the streaming grid (8 warps per SM).
+constexpr int kAttnWarpsPerSm = 8;
+constexpr size_t kAttnPartialFloats = 2 * (8 * 128 + 2 * 8);
+inline size_t attn_partial_floats(int sm_count) {
+  return (size_t)sm_count * kAttnWarpsPerSm * kAttnPartialFloats;
 }
 
 }  // namespace qq

@@ -41,8 +41,9 @@ def test_introspection_calls_need_no_gpu(lib):
     assert b"sm_100a" in lib.qq_version()
     assert lib.qq_status_string(_lib.QQ_ERR_INVALID) == b"invalid argument"
     ws = lib.qq_workspace_bytes(64, 2048, 32, 128)
-    # three counter arrays + attention partials of 64 requests x 16 chunks x 32 heads x (128 + 2) floats
-    assert ws >= 3 * 4 * _lib.QQ_MAX_BS + 4 * 64 * 16 * 32 * 130
+    # arrival counters (6 x QQ_MAX_BS int32) + two (m, l, O) records of 8 x 128 floats per
+    # streaming warp (8 warps per SM; the SM count defaults to 148 without a device)
+    assert ws >= 6 * 4 * _lib.QQ_MAX_BS + 148 * 8 * 2 * (8 * 128 + 16) * 4
 
 
 def test_argument_errors_are_reported_without_touching_a_device(lib):
