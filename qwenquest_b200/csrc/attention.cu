@@ -13,13 +13,15 @@
 //   (m, l, O), and the last warp to finish a split segment (an arrival
 //   counter in the workspace) merges it.
 // * Data movement: a warp gathers only its own KV head's 256-byte K and V
-//   slices.  Per 16-row stage each lane issues 16 cp.async.cg copies of 16
-//   bytes (one instruction = 256 B of K + 256 B of V of a row) into a private
-//   3-slot ring at a 272-byte row pitch (ldmatrix reads are bank-conflict
-//   free).  A look-ahead cursor prefetches the rows of the stage three
-//   stages beyond the newest copy into L2, so ~6 stages per warp are in
-//   flight while only 3 occupy shared memory.  Waits are per warp
-//   (cp.async.wait_group + __syncwarp): no block barrier in the loop.
+//   slices.  Per 16-row stage lane r issues one 256-byte bulk copy (the TMA
+//   engine; no multicast) of row r's K slice and lane 16 + r of its V slice,
+//   completing on the slot's mbarrier, into a private ring of slots at a
+//   272-byte row pitch (ldmatrix reads are bank-conflict free).  A
+//   look-ahead cursor prefetches the rows of the stage three stages beyond
+//   the newest copy into L2, so several more stages per warp are in flight
+//   than occupy shared memory.  Waits are per warp (bounded mbarrier waits):
+//   no block barrier in the loop.  Warps per block x slots per warp is a
+//   template parameter (8 x 3 by default).
 // * Math per stage:
 //     S^T[16 rows x 8 heads] = K[16 x 128] . Q^T[128 x 8]   (8 x mma m16n8k16)
 //     online softmax in fp32 (exp2 domain), P^T via movmatrix.trans
@@ -29,6 +31,8 @@
 // head), scores in shared memory, two-pass softmax, fp32 FMA.
 
 #include <cfloat>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 
@@ -43,15 +47,9 @@ constexpr int kH = kKV * kG;
 constexpr int kSlice = kD * 2;          // 256 bytes: one KV head of one row
 constexpr int kPitch = kSlice + 16;     // 272
 constexpr int kToks = 16;               // rows per stage (the MMA's M)
-constexpr int kSlots = 3;               // stages in a warp's shared-memory ring
 constexpr int kLookahead = 3;           // L2 prefetch distance beyond the newest copy, in stages
 constexpr int kMinShare = 64;           // rows per warp at least
-constexpr int kWarpsFast = kAttnWarpsPerSm;
-constexpr int kThreadsFast = kWarpsFast * 32;
 constexpr int kSlotBytes = 2 * kToks * kPitch;  // K slice tile + V slice tile: 8704
-constexpr int kWarpSmem = kSlots * kSlotBytes;  // 26112
-constexpr size_t kSmemRing = (size_t)kWarpsFast * kWarpSmem;            // 208896
-constexpr size_t kSmemFast = kSmemRing + sizeof(int32_t) * (QQ_MAX_BS + 1);  // + segment prefix
 constexpr int kPartFloats = kG * kD + 2 * kG;   // one partial record: O [8][128], (m, l) [8]
 
 struct AttnArgs {
@@ -224,18 +222,36 @@ __device__ __forceinline__ int64_t checked_row(const AttnArgs& a, int32_t row, b
   return valid ? row : 0;
 }
 
-// Gather the head slices of the stage's rows into `slot`: per row one warp
-// instruction, lanes 0-15 K bytes [16 l, 16 l + 16), lanes 16-31 V.
-__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, int32_t row_l, char* slot, int lane) {
-  const int64_t my_row = checked_row(a, row_l, lane < w.cnt);
-  const bool is_v = lane >= 16;
-  const int off = (lane & 15) * 16;
-  const char* src0 = (is_v ? a.v_pool : a.k_pool) + w.s_head * kSlice + off;
-  char* dst0 = slot + (is_v ? kToks * kPitch : 0) + off;
-#pragma unroll
-  for (int k = 0; k < kToks; ++k) {
-    const int64_t row = __shfl_sync(0xffffffffu, my_row, k);
-    cp_async_16(dst0 + k * kPitch, src0 + row * a.row_stride_bytes, k < w.cnt ? 16u : 0u);
+// Gather the head slices of the stage's rows into `slot` with the bulk-copy
+// (TMA) engine: lane r < 16 copies the 256-byte K slice of row r, lane 16 + r
+// the V slice, completing on the slot's mbarrier.  Rows past the end are
+// zeroed with ordinary stores (so 0 * V stays 0), ordered before later bulk
+// writes into the slot by a proxy fence.
+__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, int32_t row_l, char* slot,
+                                            uint64_t* bar, int lane) {
+  const int cnt = w.cnt;
+  const int64_t my_row = checked_row(a, row_l, lane < cnt);
+  const int64_t row = __shfl_sync(0xffffffffu, my_row, lane & 15);
+  if (cnt < kToks) {
+    constexpr int kChunks = kSlice / 16;  // 16-byte chunks per slice
+    for (int e = lane; e < (kToks - cnt) * 2 * kChunks; e += 32) {
+      const int rr = cnt + e / (2 * kChunks);
+      const int rem = e - (rr - cnt) * 2 * kChunks;
+      const int tile = rem / kChunks, ch = rem - tile * kChunks;
+      *reinterpret_cast<uint4*>(slot + tile * (kToks * kPitch) + rr * kPitch + ch * 16) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  // order this warp's earlier generic accesses to the slot (ldmatrix reads of
+  // its previous stage, zero stores) before the bulk writes below
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)cnt * 2u * kSlice);
+  __syncwarp();
+  const int r = lane & 15;
+  if (r < cnt) {
+    const bool is_v = lane >= 16;
+    const char* src = (is_v ? a.v_pool : a.k_pool) + row * a.row_stride_bytes + w.s_head * kSlice;
+    bulk_g2s(slot + (is_v ? kToks * kPitch : 0) + r * kPitch, src, kSlice, bar);
   }
 }
 
@@ -252,11 +268,28 @@ __device__ __forceinline__ void prefetch_stage(const AttnArgs& a, const Walk& w,
   }
 }
 
-__global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a) {
+template <int WARPS, int SLOTS>
+struct StreamCfg {
+  static constexpr int kThreads = WARPS * 32;
+  static constexpr size_t kRing = (size_t)WARPS * SLOTS * kSlotBytes;
+  static constexpr size_t kBars = (size_t)WARPS * SLOTS * sizeof(uint64_t);
+  static constexpr size_t kSmem = kRing + kBars + sizeof(int32_t) * (QQ_MAX_BS + 1);
+};
+
+template <int WARPS, int SLOTS>
+__global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) {
+  using Cfg = StreamCfg<WARPS, SLOTS>;
   extern __shared__ __align__(128) char smem[];
-  int32_t* s_prefix4 = reinterpret_cast<int32_t*>(smem + kSmemRing);
+  uint64_t* s_bars = reinterpret_cast<uint64_t*>(smem + Cfg::kRing);
+  int32_t* s_prefix4 = reinterpret_cast<int32_t*>(smem + Cfg::kRing + Cfg::kBars);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
+  char* ring = smem + (size_t)warp * SLOTS * kSlotBytes;
+  uint64_t* bars = s_bars + warp * SLOTS;
+  if (lane == 0) {
+    for (int s = 0; s < SLOTS; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
 
   // segment prefix 4 * P_i over the batch (warp 0, 32 requests at a time)
   if (warp == 0) {
@@ -286,12 +319,10 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a
   sp.bs = a.bs;
   sp.T = s_prefix4[a.bs];
   if (sp.T == 0) return;
-  const int grid_warps = gridDim.x * kWarpsFast;
+  const int grid_warps = gridDim.x * WARPS;
   sp.NW = (int)min((int64_t)grid_warps, max((int64_t)1, sp.T / kMinShare));
-  const int W = blockIdx.x * kWarpsFast + warp;
+  const int W = blockIdx.x * WARPS + warp;
   if (W >= sp.NW) return;
-
-  char* ring = smem + (size_t)warp * kWarpSmem;
   const __nv_bfloat16* qbase = static_cast<const __nv_bfloat16*>(a.q);
 
   // cursors: pc prefetches into L2, fc copies into the ring, cc computes
@@ -302,24 +333,24 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a
   const int64_t share_begin = pc.pos;
   bool have_p = walk_next(sp, pc);
   int32_t row_p = have_p ? stage_row(a, pc, lane) : 0;
-  for (int s = 0; s < kSlots - 1 + kLookahead && have_p; ++s) {
+  for (int s = 0; s < SLOTS - 1 + kLookahead && have_p; ++s) {
     prefetch_stage(a, pc, row_p, lane);
     have_p = walk_next(sp, pc);
     row_p = have_p ? stage_row(a, pc, lane) : 0;
   }
   bool have_f = walk_next(sp, fc);
 #pragma unroll
-  for (int s = 0; s < kSlots - 1; ++s) {
+  for (int s = 0; s < SLOTS - 1; ++s) {
     if (have_f) {
-      issue_stage(a, fc, stage_row(a, fc, lane), ring + s * kSlotBytes, lane);
+      issue_stage(a, fc, stage_row(a, fc, lane), ring + s * kSlotBytes, &bars[s], lane);
       have_f = walk_next(sp, fc);
     }
-    cp_async_commit();
   }
 
   uint32_t qb[8][2];
   float acc[8][4];
   float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
+  uint32_t phases = 0;  // bit s: parity of slot s's next completion
   int g = 0;
   while (walk_next(sp, cc)) {
     if (cc.s_first) {
@@ -337,13 +368,18 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a
       m_a = m_b = kNegInf;
       l_a = l_b = 0.f;
     }
-    cp_async_wait<kSlots - 2>();
-    __syncwarp();  // stage g visible to every lane; the slot of stage g - 1 is free
+    const int slot = g % SLOTS;
+    if (!mbar_wait(&bars[slot], (phases >> slot) & 1u)) {
+      raise_error(a.err, QQ_DEV_ERR_TIMEOUT);
+      return;
+    }
+    phases ^= 1u << slot;
+    __syncwarp();
     if (have_f) {
-      issue_stage(a, fc, stage_row(a, fc, lane), ring + ((g + kSlots - 1) % kSlots) * kSlotBytes, lane);
+      const int ns = (g + SLOTS - 1) % SLOTS;  // the slot of stage g - 1, read last iteration
+      issue_stage(a, fc, stage_row(a, fc, lane), ring + ns * kSlotBytes, &bars[ns], lane);
       have_f = walk_next(sp, fc);
     }
-    cp_async_commit();
     if (have_p) {
       prefetch_stage(a, pc, row_p, lane);
       have_p = walk_next(sp, pc);
@@ -351,7 +387,7 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a
     }
 
     const int ntok = cc.cnt;
-    const char* sk = ring + (g % kSlots) * kSlotBytes;
+    const char* sk = ring + slot * kSlotBytes;
     const char* sv = sk + kToks * kPitch;
     // ---- S^T = K . Q^T
     float c[4] = {0.f, 0.f, 0.f, 0.f};
@@ -438,8 +474,8 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a
       continue;
     }
     // split segment: record (m, l, O) in slot 0 (the share's first segment) or 1
-    const int slot = seg0 <= share_begin ? 0 : 1;
-    float* rec = a.part + ((int64_t)W * 2 + slot) * kPartFloats;
+    const int rslot = seg0 <= share_begin ? 0 : 1;
+    float* rec = a.part + ((int64_t)W * 2 + rslot) * kPartFloats;
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
       const int d0 = mt * 16 + gid;
@@ -463,50 +499,58 @@ __global__ void __launch_bounds__(kThreadsFast, 1) attn_stream_kernel(AttnArgs a
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old != w_last - w_first) continue;
 
-    // the last warp of the segment merges its records: lane -> head lane / 4,
-    // channels [32 (lane % 4), 32 (lane % 4) + 32)
+    // the last warp of the segment merges the records: lane -> query head
+    // lane / 4, channels [32 (lane % 4), 32 (lane % 4) + 32), in two halves
     __threadfence();
     if (lane == 0) a.seg_count[seg_id] = 0;
-    const int hq = lane >> 2, c0 = (lane & 3) * 32;
+    const int hq = lane >> 2;
     float M = kNegInf;
     for (int w = w_first; w <= w_last; ++w) {
       const int sl = (w == w_first && sp.begin(w_first) != seg0) ? 1 : 0;
-      const float* r2 = a.part + ((int64_t)w * 2 + sl) * kPartFloats + kG * kD;
-      M = fmaxf(M, __ldcg(r2 + hq * 2));
+      M = fmaxf(M, __ldcg(a.part + ((int64_t)w * 2 + sl) * kPartFloats + kG * kD + hq * 2));
     }
     float S = 0.f;
-    float o[32];
-#pragma unroll
-    for (int e = 0; e < 32; ++e) o[e] = 0.f;
     for (int w = w_first; w <= w_last; ++w) {
       const int sl = (w == w_first && sp.begin(w_first) != seg0) ? 1 : 0;
-      const float* r2 = a.part + ((int64_t)w * 2 + sl) * kPartFloats;
-      const float mw = __ldcg(r2 + kG * kD + hq * 2);
-      const float f = mw == kNegInf ? 0.f : fast_exp2(mw - M);
-      S += __ldcg(r2 + kG * kD + hq * 2 + 1) * f;
-      const float4* src = reinterpret_cast<const float4*>(r2 + hq * kD + c0);
-#pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        const float4 x = __ldcg(src + v);
-        o[4 * v] += f * x.x;
-        o[4 * v + 1] += f * x.y;
-        o[4 * v + 2] += f * x.z;
-        o[4 * v + 3] += f * x.w;
-      }
+      const float* ml = a.part + ((int64_t)w * 2 + sl) * kPartFloats + kG * kD + hq * 2;
+      const float mw = __ldcg(ml);
+      S += mw == kNegInf ? 0.f : __ldcg(ml + 1) * fast_exp2(mw - M);
     }
     const float inv = 1.f / S;
-    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)cc.s_req * a.out_stride +
-                         (cc.s_head * kG + hq) * kD + c0;
 #pragma unroll
-    for (int e = 0; e < 32; e += 2) {
-      __nv_bfloat162 pr;
-      pr.x = __float2bfloat16_rn(o[e] * inv);
-      pr.y = __float2bfloat16_rn(o[e + 1] * inv);
-      *reinterpret_cast<__nv_bfloat162*>(out + e) = pr;
+    for (int hf = 0; hf < 2; ++hf) {
+      const int c0 = (lane & 3) * 32 + hf * 16;
+      float o[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) o[e] = 0.f;
+      for (int w = w_first; w <= w_last; ++w) {
+        const int sl = (w == w_first && sp.begin(w_first) != seg0) ? 1 : 0;
+        const float* rw = a.part + ((int64_t)w * 2 + sl) * kPartFloats;
+        const float mw = __ldcg(rw + kG * kD + hq * 2);
+        const float f = mw == kNegInf ? 0.f : fast_exp2(mw - M);
+        const float4* src = reinterpret_cast<const float4*>(rw + hq * kD + c0);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float4 x = __ldcg(src + v);
+          o[4 * v] += f * x.x;
+          o[4 * v + 1] += f * x.y;
+          o[4 * v + 2] += f * x.z;
+          o[4 * v + 3] += f * x.w;
+        }
+      }
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)cc.s_req * a.out_stride +
+                           (cc.s_head * kG + hq) * kD + c0;
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) {
+        __nv_bfloat162 pr;
+        pr.x = __float2bfloat16_rn(o[e] * inv);
+        pr.y = __float2bfloat16_rn(o[e + 1] * inv);
+        *reinterpret_cast<__nv_bfloat162*>(out + e) = pr;
+      }
     }
   }
-  cp_async_wait<0>();
 }
+
 
 // ------------------------------------------------------------------ generic path
 
@@ -584,6 +628,48 @@ int sm_count() {
 }  // namespace
 }  // namespace qq
 
+namespace qq {
+namespace {
+
+template <int WARPS, int SLOTS>
+int launch_stream_variant(const AttnArgs& a, cudaStream_t s) {
+  using Cfg = StreamCfg<WARPS, SLOTS>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(attn_stream_kernel<WARPS, SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)Cfg::kSmem) != cudaSuccess)
+      return QQ_ERR_CUDA;
+    attr_set = true;
+  }
+  attn_stream_kernel<WARPS, SLOTS><<<sm_count(), Cfg::kThreads, Cfg::kSmem, s>>>(a);
+  return launch_status();
+}
+
+// Warps per block x ring slots per warp.  QQ_ATTN_VARIANT (e.g. "12x2") picks
+// another instantiation for tuning sweeps; the default is the measured best.
+int launch_stream(const AttnArgs& a, cudaStream_t s) {
+  static int variant = -1;
+  if (variant < 0) {
+    const char* v = getenv("QQ_ATTN_VARIANT");
+    variant = 0;
+    if (v != nullptr) {
+      if (!strcmp(v, "8x3")) variant = 1;
+      else if (!strcmp(v, "12x2")) variant = 2;
+      else if (!strcmp(v, "10x2")) variant = 3;
+      else if (!strcmp(v, "16x1")) variant = 4;
+    }
+  }
+  switch (variant) {
+    case 2: return launch_stream_variant<12, 2>(a, s);
+    case 3: return launch_stream_variant<10, 2>(a, s);
+    case 4: return launch_stream_variant<16, 1>(a, s);
+    default: return launch_stream_variant<8, 3>(a, s);
+  }
+}
+
+}  // namespace
+}  // namespace qq
+
 using namespace qq;
 
 extern "C" size_t qq_workspace_bytes(int max_bs, int top_k, int q_heads, int head_dim) {
@@ -632,17 +718,7 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
                     (reinterpret_cast<uintptr_t>(v_pool) % 16) == 0 && (q_stride % 2) == 0 &&
                     (out_stride % 2) == 0 && (reinterpret_cast<uintptr_t>(out) % 4) == 0 &&
                     (int64_t)batch->bs * top_k * kKV < (1ll << 31);
-  if (fast) {
-    static bool attr_set = false;
-    if (!attr_set) {
-      if (cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemFast) !=
-          cudaSuccess)
-        return QQ_ERR_CUDA;
-      attr_set = true;
-    }
-    attn_stream_kernel<<<sm_count(), kThreadsFast, kSmemFast, s>>>(a);
-    return launch_status();
-  }
+  if (fast) return launch_stream(a, s);
   const int G = q_heads / kv_heads;
   const size_t smem = sizeof(float) * ((size_t)G * head_dim + (size_t)G * top_k + 2 * (size_t)G);
   if (smem > 200 * 1024) return QQ_ERR_UNSUPPORTED;

@@ -162,8 +162,8 @@ inline int32_t* ws_counters(void* ws, CounterSlot slot) {
 constexpr size_t kPartialOffset = 6 * kCounterBytes;
 
 // Attention partials: two (m, l, O) records of 8 query heads x 128 channels
-// per warp of the streaming grid (8 warps per SM).
-constexpr int kAttnWarpsPerSm = 8;
+// per warp of the streaming grid (at most 16 warps per SM).
+constexpr int kAttnWarpsPerSm = 16;  // upper bound over the streaming kernel variants
 constexpr size_t kAttnPartialFloats = 2 * (8 * 128 + 2 * 8);
 inline size_t attn_partial_floats(int sm_count) {
   return (size_t)sm_count * kAttnWarpsPerSm * kAttnPartialFloats;
