@@ -13,15 +13,14 @@
 //   (m, l, O), and the last warp to finish a split segment (an arrival
 //   counter in the workspace) merges it.
 // * Data movement: a warp gathers only its own KV head's 256-byte K and V
-//   slices.  Per 16-row stage lane r issues one 256-byte bulk copy (the TMA
-//   engine; no multicast) of row r's K slice and lane 16 + r of its V slice,
-//   completing on the slot's mbarrier, into a private ring of slots at a
-//   272-byte row pitch (ldmatrix reads are bank-conflict free).  A
-//   look-ahead cursor prefetches the rows of the stage three stages beyond
-//   the newest copy into L2, so several more stages per warp are in flight
-//   than occupy shared memory.  Waits are per warp (bounded mbarrier waits):
-//   no block barrier in the loop.  Warps per block x slots per warp is a
-//   template parameter (8 x 3 by default).
+//   slices.  Per 16-row stage every lane issues 16-byte cp.async copies
+//   (one commit group per stage) into a private ring of slots at a 272-byte
+//   row pitch (ldmatrix reads are bank-conflict free).  A look-ahead cursor
+//   prefetches the rows of the stage LOOKAHEAD stages beyond the newest copy
+//   into L2, so more stages per warp are in flight than occupy shared
+//   memory.  Waits are per warp (cp.async.wait_group): no block barrier in
+//   the loop.  Warps per block x slots per warp x look-ahead are template
+//   parameters (8 x 3 x 3 by default).
 // * Math per stage:
 //     S^T[16 rows x 8 heads] = K[16 x 128] . Q^T[128 x 8]   (8 x mma m16n8k16)
 //     online softmax in fp32 (exp2 domain), P^T via movmatrix.trans
@@ -47,7 +46,7 @@ constexpr int kH = kKV * kG;
 constexpr int kSlice = kD * 2;          // 256 bytes: one KV head of one row
 constexpr int kPitch = kSlice + 16;     // 272
 constexpr int kToks = 16;               // rows per stage (the MMA's M)
-constexpr int kLookahead = 3;           // L2 prefetch distance beyond the newest copy, in stages
+
 constexpr int kMinShare = 64;           // rows per warp at least
 constexpr int kSlotBytes = 2 * kToks * kPitch;  // K slice tile + V slice tile: 8704
 constexpr int kPartFloats = kG * kD + 2 * kG;   // one partial record: O [8][128], (m, l) [8]
@@ -222,36 +221,20 @@ __device__ __forceinline__ int64_t checked_row(const AttnArgs& a, int32_t row, b
   return valid ? row : 0;
 }
 
-// Gather the head slices of the stage's rows into `slot` with the bulk-copy
-// (TMA) engine: lane r < 16 copies the 256-byte K slice of row r, lane 16 + r
-// the V slice, completing on the slot's mbarrier.  Rows past the end are
-// zeroed with ordinary stores (so 0 * V stays 0), ordered before later bulk
-// writes into the slot by a proxy fence.
-__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, int32_t row_l, char* slot,
-                                            uint64_t* bar, int lane) {
-  const int cnt = w.cnt;
-  const int64_t my_row = checked_row(a, row_l, lane < cnt);
-  const int64_t row = __shfl_sync(0xffffffffu, my_row, lane & 15);
-  if (cnt < kToks) {
-    constexpr int kChunks = kSlice / 16;  // 16-byte chunks per slice
-    for (int e = lane; e < (kToks - cnt) * 2 * kChunks; e += 32) {
-      const int rr = cnt + e / (2 * kChunks);
-      const int rem = e - (rr - cnt) * 2 * kChunks;
-      const int tile = rem / kChunks, ch = rem - tile * kChunks;
-      *reinterpret_cast<uint4*>(slot + tile * (kToks * kPitch) + rr * kPitch + ch * 16) = make_uint4(0, 0, 0, 0);
-    }
-  }
-  // order this warp's earlier generic accesses to the slot (ldmatrix reads of
-  // its previous stage, zero stores) before the bulk writes below
-  fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)cnt * 2u * kSlice);
-  __syncwarp();
-  const int r = lane & 15;
-  if (r < cnt) {
-    const bool is_v = lane >= 16;
-    const char* src = (is_v ? a.v_pool : a.k_pool) + row * a.row_stride_bytes + w.s_head * kSlice;
-    bulk_g2s(slot + (is_v ? kToks * kPitch : 0) + r * kPitch, src, kSlice, bar);
+// Gather the head slices of the stage's rows into `slot`: per row one warp
+// instruction of 16-byte cp.async.cg copies, lanes 0-15 K bytes [16 l, 16 l + 16),
+// lanes 16-31 V; rows past the end are zero-filled by the copy (0 * V stays 0).
+// (256-byte bulk copies on an mbarrier measured slower for this gather.)
+__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, int32_t row_l, char* slot, int lane) {
+  const int64_t my_row = checked_row(a, row_l, lane < w.cnt);
+  const bool is_v = lane >= 16;
+  const int off = (lane & 15) * 16;
+  const char* src0 = (is_v ? a.v_pool : a.k_pool) + w.s_head * kSlice + off;
+  char* dst0 = slot + (is_v ? kToks * kPitch : 0) + off;
+#pragma unroll
+  for (int k = 0; k < kToks; ++k) {
+    const int64_t row = __shfl_sync(0xffffffffu, my_row, k);
+    cp_async_16(dst0 + k * kPitch, src0 + row * a.row_stride_bytes, k < w.cnt ? 16u : 0u);
   }
 }
 
@@ -270,26 +253,20 @@ __device__ __forceinline__ void prefetch_stage(const AttnArgs& a, const Walk& w,
 
 template <int WARPS, int SLOTS>
 struct StreamCfg {
+  static_assert(SLOTS >= 2, "the ring overlaps the copy of one stage with the math of another");
   static constexpr int kThreads = WARPS * 32;
   static constexpr size_t kRing = (size_t)WARPS * SLOTS * kSlotBytes;
-  static constexpr size_t kBars = (size_t)WARPS * SLOTS * sizeof(uint64_t);
-  static constexpr size_t kSmem = kRing + kBars + sizeof(int32_t) * (QQ_MAX_BS + 1);
+  static constexpr size_t kSmem = kRing + sizeof(int32_t) * (QQ_MAX_BS + 1);
 };
 
-template <int WARPS, int SLOTS>
+template <int WARPS, int SLOTS, int LOOKAHEAD>
 __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) {
   using Cfg = StreamCfg<WARPS, SLOTS>;
   extern __shared__ __align__(128) char smem[];
-  uint64_t* s_bars = reinterpret_cast<uint64_t*>(smem + Cfg::kRing);
-  int32_t* s_prefix4 = reinterpret_cast<int32_t*>(smem + Cfg::kRing + Cfg::kBars);
+  int32_t* s_prefix4 = reinterpret_cast<int32_t*>(smem + Cfg::kRing);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
   char* ring = smem + (size_t)warp * SLOTS * kSlotBytes;
-  uint64_t* bars = s_bars + warp * SLOTS;
-  if (lane == 0) {
-    for (int s = 0; s < SLOTS; ++s) mbar_init(&bars[s], 1);
-    fence_mbar_init();
-  }
 
   // segment prefix 4 * P_i over the batch (warp 0, 32 requests at a time)
   if (warp == 0) {
@@ -333,7 +310,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
   const int64_t share_begin = pc.pos;
   bool have_p = walk_next(sp, pc);
   int32_t row_p = have_p ? stage_row(a, pc, lane) : 0;
-  for (int s = 0; s < SLOTS - 1 + kLookahead && have_p; ++s) {
+  for (int s = 0; s < SLOTS - 1 + LOOKAHEAD && have_p; ++s) {
     prefetch_stage(a, pc, row_p, lane);
     have_p = walk_next(sp, pc);
     row_p = have_p ? stage_row(a, pc, lane) : 0;
@@ -342,15 +319,15 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
 #pragma unroll
   for (int s = 0; s < SLOTS - 1; ++s) {
     if (have_f) {
-      issue_stage(a, fc, stage_row(a, fc, lane), ring + s * kSlotBytes, &bars[s], lane);
+      issue_stage(a, fc, stage_row(a, fc, lane), ring + s * kSlotBytes, lane);
       have_f = walk_next(sp, fc);
     }
+    cp_async_commit();
   }
 
   uint32_t qb[8][2];
   float acc[8][4];
   float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
-  uint32_t phases = 0;  // bit s: parity of slot s's next completion
   int g = 0;
   while (walk_next(sp, cc)) {
     if (cc.s_first) {
@@ -369,17 +346,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       l_a = l_b = 0.f;
     }
     const int slot = g % SLOTS;
-    if (!mbar_wait(&bars[slot], (phases >> slot) & 1u)) {
-      raise_error(a.err, QQ_DEV_ERR_TIMEOUT);
-      return;
-    }
-    phases ^= 1u << slot;
-    __syncwarp();
+    cp_async_wait<SLOTS - 2>();
+    __syncwarp();  // stage g visible to every lane; the slot of stage g - 1 is free
     if (have_f) {
-      const int ns = (g + SLOTS - 1) % SLOTS;  // the slot of stage g - 1, read last iteration
-      issue_stage(a, fc, stage_row(a, fc, lane), ring + ns * kSlotBytes, &bars[ns], lane);
+      const int ns = (g + SLOTS - 1) % SLOTS;
+      issue_stage(a, fc, stage_row(a, fc, lane), ring + ns * kSlotBytes, lane);
       have_f = walk_next(sp, fc);
     }
+    cp_async_commit();
     if (have_p) {
       prefetch_stage(a, pc, row_p, lane);
       have_p = walk_next(sp, pc);
@@ -549,8 +523,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       }
     }
   }
+  cp_async_wait<0>();
 }
-
 
 // ------------------------------------------------------------------ generic path
 
@@ -631,39 +605,44 @@ int sm_count() {
 namespace qq {
 namespace {
 
-template <int WARPS, int SLOTS>
+template <int WARPS, int SLOTS, int LOOKAHEAD>
 int launch_stream_variant(const AttnArgs& a, cudaStream_t s) {
   using Cfg = StreamCfg<WARPS, SLOTS>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(attn_stream_kernel<WARPS, SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)Cfg::kSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_stream_kernel<WARPS, SLOTS, LOOKAHEAD>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem) != cudaSuccess)
       return QQ_ERR_CUDA;
     attr_set = true;
   }
-  attn_stream_kernel<WARPS, SLOTS><<<sm_count(), Cfg::kThreads, Cfg::kSmem, s>>>(a);
+  attn_stream_kernel<WARPS, SLOTS, LOOKAHEAD><<<sm_count(), Cfg::kThreads, Cfg::kSmem, s>>>(a);
   return launch_status();
 }
 
-// Warps per block x ring slots per warp.  QQ_ATTN_VARIANT (e.g. "12x2") picks
-// another instantiation for tuning sweeps; the default is the measured best.
+// Warps per block x ring slots per warp x L2 look-ahead stages.
+// QQ_ATTN_VARIANT (e.g. "12x2x3") picks another instantiation for tuning
+// sweeps; the default is the measured best.
 int launch_stream(const AttnArgs& a, cudaStream_t s) {
   static int variant = -1;
   if (variant < 0) {
     const char* v = getenv("QQ_ATTN_VARIANT");
     variant = 0;
     if (v != nullptr) {
-      if (!strcmp(v, "8x3")) variant = 1;
-      else if (!strcmp(v, "12x2")) variant = 2;
-      else if (!strcmp(v, "10x2")) variant = 3;
-      else if (!strcmp(v, "16x1")) variant = 4;
+      if (!strcmp(v, "8x3x3")) variant = 1;
+      else if (!strcmp(v, "12x2x3")) variant = 2;
+      else if (!strcmp(v, "10x2x3")) variant = 3;
+      else if (!strcmp(v, "8x3x6")) variant = 4;
+      else if (!strcmp(v, "12x2x6")) variant = 5;
+      else if (!strcmp(v, "8x3x0")) variant = 6;
     }
   }
   switch (variant) {
-    case 2: return launch_stream_variant<12, 2>(a, s);
-    case 3: return launch_stream_variant<10, 2>(a, s);
-    case 4: return launch_stream_variant<16, 1>(a, s);
-    default: return launch_stream_variant<8, 3>(a, s);
+    case 2: return launch_stream_variant<12, 2, 3>(a, s);
+    case 3: return launch_stream_variant<10, 2, 3>(a, s);
+    case 4: return launch_stream_variant<8, 3, 6>(a, s);
+    case 5: return launch_stream_variant<12, 2, 6>(a, s);
+    case 6: return launch_stream_variant<8, 3, 0>(a, s);
+    default: return launch_stream_variant<8, 3, 3>(a, s);
   }
 }
 
