@@ -13,14 +13,12 @@
 //   (m, l, O), and the last warp to finish a split segment (an arrival
 //   counter in the workspace) merges it.
 // * Data movement: a warp gathers only its own KV head's 256-byte K and V
-//   slices.  Per 16-row stage every lane issues 16-byte cp.async copies
-//   (one commit group per stage) into a private ring of slots at a 272-byte
-//   row pitch (ldmatrix reads are bank-conflict free).  A look-ahead cursor
-//   prefetches the rows of the stage LOOKAHEAD stages beyond the newest copy
-//   into L2, so more stages per warp are in flight than occupy shared
-//   memory.  Waits are per warp (cp.async.wait_group): no block barrier in
-//   the loop.  Warps per block x slots per warp x look-ahead are template
-//   parameters (8 x 3 x 3 by default).
+//   slices.  Per 16-row stage every lane reads the stage's 16 row indices
+//   (four broadcast int4 loads) and issues 16 16-byte cp.async copies (one
+//   commit group per stage) into a private ring of slots at a 272-byte row
+//   pitch (ldmatrix reads are bank-conflict free).  Waits are per warp
+//   (cp.async.wait_group): no block barrier in the loop.  Warps per block x
+//   slots per warp are template parameters (8 x 3 by default).
 // * Math per stage:
 //     S^T[16 rows x 8 heads] = K[16 x 128] . Q^T[128 x 8]   (8 x mma m16n8k16)
 //     online softmax in fp32 (exp2 domain), P^T via movmatrix.trans
@@ -100,25 +98,25 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return y;
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  const uint32_t l = f32_to_bf16_bits(lo), h = f32_to_bf16_bits(hi);
-  return (h << 16) | l;
+__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 x) {
+  return *reinterpret_cast<const uint32_t*>(&x);
 }
 
-// Packs bf16(lo), bf16(hi) and returns the rounded values as floats.
-__device__ __forceinline__ uint32_t pack_bf16x2_split(float lo, float hi, float& lo_r, float& hi_r) {
-  const uint32_t l = f32_to_bf16_bits(lo), h = f32_to_bf16_bits(hi);
-  lo_r = bf16_bits_to_f32(l);
-  hi_r = bf16_bits_to_f32(h);
-  return (h << 16) | l;
+// 2^x by the hardware approximation (ex2.approx.ftz: relative error ~2^-22,
+// results below 2^-126 flush to 0, 2^-inf = 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
-
-// 16-byte async copy global -> shared; src_bytes = 0 writes zeros.
-__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
-               "r"(src_bytes)
+// 16-byte async copy global -> shared (L2 only).
+__device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gmem_src) : "memory");
+}
+// The same with a source size: the bytes past src_bytes (all 16 for 0) are written as zeros.
+__device__ __forceinline__ void cp_async_16_zfill(uint32_t smem_dst, const void* gmem_src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_dst), "l"(gmem_src), "r"(src_bytes)
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -127,65 +125,75 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
 #define kNegInf (-__int_as_float(0x7f800000))
 
 // ------------------------------------------------------------------ stream-K walk
 //
 // Flattened position p in [0, T), T = 4 * sum_i n_i: segment (i, h) covers
 // [4 P_i + h n_i, 4 P_i + (h + 1) n_i) with P_i = sum_{j<i} n_j.  Warp w of
-// NW owns [B(w), B(w + 1)), B(w) = floor(w T / NW).
+// NW owns [B(w), B(w + 1)), B(w) = floor(w T / NW) moved down to a 16-row
+// stage boundary of its segment, so every stage starts at a multiple of 16
+// rows into its segment (its row indices are four aligned int4 loads).  The
+// fast path requires T < 2^31 (positions are int32).
 
 struct Split {
   const int32_t* prefix4;  // shared: 4 * P_i, i = 0..bs
   int bs;
-  int64_t T;
+  int T;
   int NW;
-  __device__ __forceinline__ int64_t begin(int w) const { return (int64_t)w * T / NW; }
-  // warp owning position p
-  __device__ __forceinline__ int owner(int64_t p) const { return (int)(((p + 1) * NW - 1) / T); }
+  // segment containing p: largest i with prefix4[i] <= p, then the head
+  __device__ __forceinline__ void seek(int p, int& req, int& head, int& n, int& seg_start) const {
+    int lo = 0, hi = bs;  // prefix4[lo] <= p < prefix4[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (prefix4[mid] <= p) lo = mid; else hi = mid;
+    }
+    req = lo;
+    n = (prefix4[lo + 1] - prefix4[lo]) >> 2;
+    head = (p - prefix4[lo]) / n;
+    seg_start = prefix4[lo] + head * n;
+  }
+  __device__ __forceinline__ int begin(int w) const {
+    if (w >= NW) return T;
+    const int raw = (int)((int64_t)w * T / NW);
+    if (raw == 0) return 0;
+    int req, head, n, s0;
+    seek(raw, req, head, n, s0);
+    return s0 + ((raw - s0) & ~(kToks - 1));
+  }
+  // warp owning position p.  Shares are >= 64 rows before alignment, so the
+  // aligned owner is the unaligned one or the next warp.
+  __device__ __forceinline__ int owner(int p) const {
+    int w = (int)(((int64_t)(p + 1) * NW - 1) / T);
+    if (w + 1 < NW && begin(w + 1) <= p) ++w;
+    return w;
+  }
 };
 
 struct Walk {
-  int64_t begin;           // start of the share
-  int64_t pos, end;        // next position to issue, end of the share
+  int begin;               // start of the share
+  int pos, end;            // next position to issue, end of the share
   int req, head, n;        // current segment
-  int64_t seg_start;
+  int seg_start;
   // the stage last produced by next():
-  int r0, cnt;             // rows [r0, r0 + cnt) of segment (req, head)
-  int64_t stage_seg_start;
+  int r0, cnt;             // rows [r0, r0 + cnt) of segment (req, head); r0 % 16 == 0
+  int stage_seg_start;
   int s_req, s_head, s_n;
   bool s_first, s_last;    // stage opens / closes this warp's portion of the segment
 };
 
-__device__ __forceinline__ void walk_seek(const Split& sp, Walk& w, int64_t p) {
-  // segment containing p: largest i with prefix4[i] <= p, then the head
-  int lo = 0, hi = sp.bs;  // prefix4[lo] <= p < prefix4[hi]
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (sp.prefix4[mid] <= p) lo = mid; else hi = mid;
-  }
-  w.req = lo;
-  w.n = (sp.prefix4[lo + 1] - sp.prefix4[lo]) >> 2;
-  w.head = (int)((p - sp.prefix4[lo]) / w.n);
-  w.seg_start = sp.prefix4[lo] + (int64_t)w.head * w.n;
-}
-
 __device__ __forceinline__ void walk_init(const Split& sp, Walk& w, int warp_id) {
   w.begin = w.pos = sp.begin(warp_id);
   w.end = sp.begin(warp_id + 1);
-  if (w.pos < w.end) walk_seek(sp, w, w.pos);
+  if (w.pos < w.end) sp.seek(w.pos, w.req, w.head, w.n, w.seg_start);
 }
 
 __device__ __forceinline__ bool walk_next(const Split& sp, Walk& w) {
   if (w.pos >= w.end) return false;
-  const int64_t seg_end = w.seg_start + w.n;
-  const int64_t stop = min(min(w.pos + kToks, seg_end), w.end);
-  w.r0 = (int)(w.pos - w.seg_start);
-  w.cnt = (int)(stop - w.pos);
+  const int seg_end = w.seg_start + w.n;
+  const int stop = min(min(w.pos + kToks, seg_end), w.end);
+  w.r0 = w.pos - w.seg_start;
+  w.cnt = stop - w.pos;
   w.stage_seg_start = w.seg_start;
   w.s_req = w.req;
   w.s_head = w.head;
@@ -208,46 +216,46 @@ __device__ __forceinline__ bool walk_next(const Split& sp, Walk& w) {
   return true;
 }
 
-// Lane l's pool row for row l of the walk's current stage (lanes >= cnt: 0).
-__device__ __forceinline__ int32_t stage_row(const AttnArgs& a, const Walk& w, int lane) {
-  return lane < w.cnt ? __ldg(a.rows + (int64_t)w.s_req * a.top_k + w.r0 + lane) : 0;
-}
-
-__device__ __forceinline__ int64_t checked_row(const AttnArgs& a, int32_t row, bool valid) {
-  if (valid && (row < 0 || row >= a.num_rows)) {
-    raise_error(a.err, QQ_DEV_ERR_BOUNDS);
-    return 0;
-  }
-  return valid ? row : 0;
-}
-
-// Gather the head slices of the stage's rows into `slot`: per row one warp
-// instruction of 16-byte cp.async.cg copies, lanes 0-15 K bytes [16 l, 16 l + 16),
-// lanes 16-31 V; rows past the end are zero-filled by the copy (0 * V stays 0).
+// Gather the head slices of the stage's rows into a ring slot: per row one
+// warp instruction of 16-byte cp.async.cg copies, lanes 0-15 K bytes
+// [16 l, 16 l + 16), lanes 16-31 V.  Every lane reads the stage's 16 row
+// indices with four broadcast int4 loads; a row outside [0, num_rows) raises
+// QQ_DEV_ERR_BOUNDS and is replaced by row 0.  Rows past the end of a short
+// stage are zero-filled by the copy (0 * V stays 0).
 // (256-byte bulk copies on an mbarrier measured slower for this gather.)
-__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, int32_t row_l, char* slot, int lane) {
-  const int64_t my_row = checked_row(a, row_l, lane < w.cnt);
-  const bool is_v = lane >= 16;
-  const int off = (lane & 15) * 16;
-  const char* src0 = (is_v ? a.v_pool : a.k_pool) + w.s_head * kSlice + off;
-  char* dst0 = slot + (is_v ? kToks * kPitch : 0) + off;
+__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, const char* lane_pool,
+                                            uint32_t lane_dst, uint32_t stride, uint32_t max_row) {
+  const int4* rp = reinterpret_cast<const int4*>(a.rows + (int64_t)w.s_req * a.top_k + w.r0);
+  uint32_t r[kToks];
 #pragma unroll
-  for (int k = 0; k < kToks; ++k) {
-    const int64_t row = __shfl_sync(0xffffffffu, my_row, k);
-    cp_async_16(dst0 + k * kPitch, src0 + row * a.row_stride_bytes, k < w.cnt ? 16u : 0u);
+  for (int i = 0; i < kToks / 4; ++i) {
+    const int4 x = __ldg(rp + i);
+    r[4 * i] = (uint32_t)x.x;
+    r[4 * i + 1] = (uint32_t)x.y;
+    r[4 * i + 2] = (uint32_t)x.z;
+    r[4 * i + 3] = (uint32_t)x.w;
   }
-}
-
-// L2 prefetch of the head slices of a stage's rows (two 128-byte lines of K and of V per row).
-__device__ __forceinline__ void prefetch_stage(const AttnArgs& a, const Walk& w, int32_t row_l, int lane) {
-  if (lane < w.cnt) {
-    const int64_t row = checked_row(a, row_l, true);
-    const char* kp = a.k_pool + row * a.row_stride_bytes + w.s_head * kSlice;
-    const char* vp = a.v_pool + row * a.row_stride_bytes + w.s_head * kSlice;
-    prefetch_l2(kp);
-    prefetch_l2(kp + 128);
-    prefetch_l2(vp);
-    prefetch_l2(vp + 128);
+  const bool full = w.cnt == kToks;
+  if (!full) {
+#pragma unroll
+    for (int k = 0; k < kToks; ++k) r[k] = k < w.cnt ? r[k] : 0u;
+  }
+  bool bad = false;
+#pragma unroll
+  for (int k = 0; k < kToks; ++k) bad |= r[k] > max_row;
+  if (bad) {
+    raise_error(a.err, QQ_DEV_ERR_BOUNDS);
+#pragma unroll
+    for (int k = 0; k < kToks; ++k) r[k] = r[k] > max_row ? 0u : r[k];
+  }
+  const char* src = lane_pool + w.s_head * kSlice;
+  if (full) {
+#pragma unroll
+    for (int k = 0; k < kToks; ++k) cp_async_16(lane_dst + k * kPitch, src + (size_t)r[k] * stride);
+  } else {
+#pragma unroll
+    for (int k = 0; k < kToks; ++k)
+      cp_async_16_zfill(lane_dst + k * kPitch, src + (size_t)r[k] * stride, k < w.cnt ? 16u : 0u);
   }
 }
 
@@ -259,7 +267,7 @@ struct StreamCfg {
   static constexpr size_t kSmem = kRing + sizeof(int32_t) * (QQ_MAX_BS + 1);
 };
 
-template <int WARPS, int SLOTS, int LOOKAHEAD>
+template <int WARPS, int SLOTS>
 __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) {
   using Cfg = StreamCfg<WARPS, SLOTS>;
   extern __shared__ __align__(128) char smem[];
@@ -297,44 +305,44 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
   sp.T = s_prefix4[a.bs];
   if (sp.T == 0) return;
   const int grid_warps = gridDim.x * WARPS;
-  sp.NW = (int)min((int64_t)grid_warps, max((int64_t)1, sp.T / kMinShare));
+  sp.NW = min(grid_warps, max(1, sp.T / kMinShare));
   const int W = blockIdx.x * WARPS + warp;
   if (W >= sp.NW) return;
   const __nv_bfloat16* qbase = static_cast<const __nv_bfloat16*>(a.q);
 
-  // cursors: pc prefetches into L2, fc copies into the ring, cc computes
-  Walk pc, fc, cc;
-  walk_init(sp, pc, W);
-  fc = pc;
-  cc = pc;
-  const int64_t share_begin = pc.pos;
-  bool have_p = walk_next(sp, pc);
-  int32_t row_p = have_p ? stage_row(a, pc, lane) : 0;
-  for (int s = 0; s < SLOTS - 1 + LOOKAHEAD && have_p; ++s) {
-    prefetch_stage(a, pc, row_p, lane);
-    have_p = walk_next(sp, pc);
-    row_p = have_p ? stage_row(a, pc, lane) : 0;
-  }
+  // per-lane copy constants
+  const char* lane_pool = (lane < 16 ? a.k_pool : a.v_pool) + (lane & 15) * 16;
+  const uint32_t ring_dst = smem_u32(ring) + (lane < 16 ? 0 : kToks * kPitch) + (lane & 15) * 16;
+  const uint32_t stride = (uint32_t)a.row_stride_bytes;
+  const uint32_t max_row = (uint32_t)min(a.num_rows - 1, (int64_t)INT32_MAX);
+
+  // cursors: fc copies into the ring, cc computes
+  Walk fc, cc;
+  walk_init(sp, fc, W);
+  cc = fc;
+  const int share_begin = fc.pos;
   bool have_f = walk_next(sp, fc);
+  int fslot = 0;
 #pragma unroll
   for (int s = 0; s < SLOTS - 1; ++s) {
     if (have_f) {
-      issue_stage(a, fc, stage_row(a, fc, lane), ring + s * kSlotBytes, lane);
+      issue_stage(a, fc, lane_pool, ring_dst + fslot * kSlotBytes, stride, max_row);
       have_f = walk_next(sp, fc);
     }
     cp_async_commit();
+    fslot = fslot + 1 == SLOTS ? 0 : fslot + 1;
   }
 
   uint32_t qb[8][2];
   float acc[8][4];
   float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
-  int g = 0;
+  int slot = 0;
   while (walk_next(sp, cc)) {
     if (cc.s_first) {
       // a new portion of a segment: Q^T fragments of this KV head, loaded
       // before the wait so their latency hides behind it
       const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qbase + (int64_t)cc.s_req * a.q_stride +
-                                                               (int64_t)(cc.s_head * kG + gid) * kD);
+                                                               (cc.s_head * kG + gid) * kD);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         qb[kk][0] = __ldg(qrow + (kk * 16 + 2 * tig) / 2);
@@ -345,24 +353,19 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       m_a = m_b = kNegInf;
       l_a = l_b = 0.f;
     }
-    const int slot = g % SLOTS;
     cp_async_wait<SLOTS - 2>();
-    __syncwarp();  // stage g visible to every lane; the slot of stage g - 1 is free
+    __syncwarp();  // the current stage is visible to every lane; the previous stage's slot is free
     if (have_f) {
-      const int ns = (g + SLOTS - 1) % SLOTS;
-      issue_stage(a, fc, stage_row(a, fc, lane), ring + ns * kSlotBytes, lane);
+      issue_stage(a, fc, lane_pool, ring_dst + fslot * kSlotBytes, stride, max_row);
       have_f = walk_next(sp, fc);
     }
     cp_async_commit();
-    if (have_p) {
-      prefetch_stage(a, pc, row_p, lane);
-      have_p = walk_next(sp, pc);
-      row_p = have_p ? stage_row(a, pc, lane) : 0;
-    }
+    fslot = fslot + 1 == SLOTS ? 0 : fslot + 1;
 
     const int ntok = cc.cnt;
     const char* sk = ring + slot * kSlotBytes;
     const char* sv = sk + kToks * kPitch;
+    slot = slot + 1 == SLOTS ? 0 : slot + 1;
     // ---- S^T = K . Q^T
     float c[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t kaddr = smem_u32(sk + (lane & 15) * kPitch + (lane >> 4) * 16);
@@ -385,31 +388,40 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
     }
     const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-    const float al_a = mn_a == kNegInf ? 1.f : fast_exp2(m_a - mn_a);
-    const float al_b = mn_b == kNegInf ? 1.f : fast_exp2(m_b - mn_b);
-    const float p00 = mn_a == kNegInf ? 0.f : fast_exp2(s00 - mn_a);
-    const float p10 = mn_a == kNegInf ? 0.f : fast_exp2(s10 - mn_a);
-    const float p01 = mn_b == kNegInf ? 0.f : fast_exp2(s01 - mn_b);
-    const float p11 = mn_b == kNegInf ? 0.f : fast_exp2(s11 - mn_b);
+    // a head whose running max is still -inf has seen only masked rows: its
+    // weights are 0 and its (zero) accumulator needs no rescale
+    const float base_a = mn_a == kNegInf ? 0.f : mn_a;
+    const float base_b = mn_b == kNegInf ? 0.f : mn_b;
+    const float p00 = fast_exp2(s00 - base_a), p10 = fast_exp2(s10 - base_a);
+    const float p01 = fast_exp2(s01 - base_b), p11 = fast_exp2(s11 - base_b);
+    if (__any_sync(0xffffffffu, mn_a != m_a || mn_b != m_b)) {
+      const float al_a = fast_exp2(m_a - base_a), al_b = fast_exp2(m_b - base_b);
+      l_a *= al_a;
+      l_b *= al_b;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        acc[mt][0] *= al_a;
+        acc[mt][1] *= al_b;
+        acc[mt][2] *= al_a;
+        acc[mt][3] *= al_b;
+      }
+    }
     m_a = mn_a;
     m_b = mn_b;
-    l_a = l_a * al_a + p00 + p10;
-    l_b = l_b * al_b + p01 + p11;
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      acc[mt][0] *= al_a;
-      acc[mt][1] *= al_b;
-      acc[mt][2] *= al_a;
-      acc[mt][3] *= al_b;
-    }
+    l_a += p00 + p10;
+    l_b += p01 + p11;
     // ---- P^T fragments (rows x heads -> heads x rows) and O^T += V^T . P^T,
     // P split into bf16 hi + lo parts (two MMAs per tile): the weights carry
     // ~16 mantissa bits and the fp32 result tracks an fp32 softmax-weighted sum
-    float h00, h01, h10, h11;
-    const uint32_t pb0 = movmatrix_trans(pack_bf16x2_split(p00, p01, h00, h01));
-    const uint32_t pb1 = movmatrix_trans(pack_bf16x2_split(p10, p11, h10, h11));
-    const uint32_t pl0 = movmatrix_trans(pack_bf16x2(p00 - h00, p01 - h01));
-    const uint32_t pl1 = movmatrix_trans(pack_bf16x2(p10 - h10, p11 - h11));
+    const __nv_bfloat162 h0 = __floats2bfloat162_rn(p00, p01);
+    const __nv_bfloat162 h1 = __floats2bfloat162_rn(p10, p11);
+    const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+    const __nv_bfloat162 lo0 = __floats2bfloat162_rn(p00 - f0.x, p01 - f0.y);
+    const __nv_bfloat162 lo1 = __floats2bfloat162_rn(p10 - f1.x, p11 - f1.y);
+    const uint32_t pb0 = movmatrix_trans(bf162_bits(h0));
+    const uint32_t pb1 = movmatrix_trans(bf162_bits(h1));
+    const uint32_t pl0 = movmatrix_trans(bf162_bits(lo0));
+    const uint32_t pl1 = movmatrix_trans(bf162_bits(lo1));
     const int j = lane >> 3, r = lane & 7;
     const uint32_t vaddr = smem_u32(sv + ((j >> 1) * 8 + r) * kPitch + (j & 1) * 16);
 #pragma unroll
@@ -419,7 +431,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
       mma_bf16_16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
     }
-    ++g;
     if (!cc.s_last) continue;
 
     // ---- end of this warp's portion of segment (req, head)
@@ -429,8 +440,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       la += __shfl_xor_sync(0xffffffffu, la, o);
       lb += __shfl_xor_sync(0xffffffffu, lb, o);
     }
-    const int64_t seg0 = cc.stage_seg_start;
-    const int64_t seg1 = seg0 + cc.s_n;
+    const int seg0 = cc.stage_seg_start;
+    const int seg1 = seg0 + cc.s_n;
     const int w_first = sp.owner(seg0), w_last = sp.owner(seg1 - 1);
     const int qh_a = cc.s_head * kG + 2 * tig, qh_b = qh_a + 1;  // this thread's query heads
     if (w_first == w_last) {
@@ -478,14 +489,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
     __threadfence();
     if (lane == 0) a.seg_count[seg_id] = 0;
     const int hq = lane >> 2;
+    // warp w_first holds the segment in record 1 unless its share starts at the segment
+    const int first_slot = sp.begin(w_first) != seg0 ? 1 : 0;
     float M = kNegInf;
     for (int w = w_first; w <= w_last; ++w) {
-      const int sl = (w == w_first && sp.begin(w_first) != seg0) ? 1 : 0;
+      const int sl = w == w_first ? first_slot : 0;
       M = fmaxf(M, __ldcg(a.part + ((int64_t)w * 2 + sl) * kPartFloats + kG * kD + hq * 2));
     }
     float S = 0.f;
     for (int w = w_first; w <= w_last; ++w) {
-      const int sl = (w == w_first && sp.begin(w_first) != seg0) ? 1 : 0;
+      const int sl = w == w_first ? first_slot : 0;
       const float* ml = a.part + ((int64_t)w * 2 + sl) * kPartFloats + kG * kD + hq * 2;
       const float mw = __ldcg(ml);
       S += mw == kNegInf ? 0.f : __ldcg(ml + 1) * fast_exp2(mw - M);
@@ -498,7 +511,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
 #pragma unroll
       for (int e = 0; e < 16; ++e) o[e] = 0.f;
       for (int w = w_first; w <= w_last; ++w) {
-        const int sl = (w == w_first && sp.begin(w_first) != seg0) ? 1 : 0;
+        const int sl = w == w_first ? first_slot : 0;
         const float* rw = a.part + ((int64_t)w * 2 + sl) * kPartFloats;
         const float mw = __ldcg(rw + kG * kD + hq * 2);
         const float f = mw == kNegInf ? 0.f : fast_exp2(mw - M);
@@ -605,44 +618,37 @@ int sm_count() {
 namespace qq {
 namespace {
 
-template <int WARPS, int SLOTS, int LOOKAHEAD>
+template <int WARPS, int SLOTS>
 int launch_stream_variant(const AttnArgs& a, cudaStream_t s) {
   using Cfg = StreamCfg<WARPS, SLOTS>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(attn_stream_kernel<WARPS, SLOTS, LOOKAHEAD>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_stream_kernel<WARPS, SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)Cfg::kSmem) != cudaSuccess)
       return QQ_ERR_CUDA;
     attr_set = true;
   }
-  attn_stream_kernel<WARPS, SLOTS, LOOKAHEAD><<<sm_count(), Cfg::kThreads, Cfg::kSmem, s>>>(a);
+  attn_stream_kernel<WARPS, SLOTS><<<sm_count(), Cfg::kThreads, Cfg::kSmem, s>>>(a);
   return launch_status();
 }
 
-// Warps per block x ring slots per warp x L2 look-ahead stages.
-// QQ_ATTN_VARIANT (e.g. "12x2x3") picks another instantiation for tuning
-// sweeps; the default is the measured best.
+// Warps per block x ring slots per warp.  QQ_ATTN_VARIANT (e.g. "12x2") picks
+// another instantiation for tuning sweeps; the default is the measured best.
 int launch_stream(const AttnArgs& a, cudaStream_t s) {
   static int variant = -1;
   if (variant < 0) {
     const char* v = getenv("QQ_ATTN_VARIANT");
     variant = 0;
     if (v != nullptr) {
-      if (!strcmp(v, "8x3x3")) variant = 1;
-      else if (!strcmp(v, "12x2x3")) variant = 2;
-      else if (!strcmp(v, "10x2x3")) variant = 3;
-      else if (!strcmp(v, "8x3x6")) variant = 4;
-      else if (!strcmp(v, "12x2x6")) variant = 5;
-      else if (!strcmp(v, "8x3x0")) variant = 6;
+      if (!strcmp(v, "8x3")) variant = 1;
+      else if (!strcmp(v, "12x2")) variant = 2;
+      else if (!strcmp(v, "6x4")) variant = 3;
     }
   }
   switch (variant) {
-    case 2: return launch_stream_variant<12, 2, 3>(a, s);
-    case 3: return launch_stream_variant<10, 2, 3>(a, s);
-    case 4: return launch_stream_variant<8, 3, 6>(a, s);
-    case 5: return launch_stream_variant<12, 2, 6>(a, s);
-    case 6: return launch_stream_variant<8, 3, 0>(a, s);
-    default: return launch_stream_variant<8, 3, 3>(a, s);
+    case 2: return launch_stream_variant<12, 2>(a, s);
+    case 3: return launch_stream_variant<6, 4>(a, s);
+    default: return launch_stream_variant<8, 3>(a, s);
   }
 }
 
@@ -696,7 +702,8 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
                     (kv_row_stride * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(k_pool) % 16) == 0 &&
                     (reinterpret_cast<uintptr_t>(v_pool) % 16) == 0 && (q_stride % 2) == 0 &&
                     (out_stride % 2) == 0 && (reinterpret_cast<uintptr_t>(out) % 4) == 0 &&
-                    (int64_t)batch->bs * top_k * kKV < (1ll << 31);
+                    (int64_t)batch->bs * top_k * kKV < (1ll << 31) && top_k % kToks == 0 &&
+                    (reinterpret_cast<uintptr_t>(rows) % 16) == 0 && kv_row_stride * esz < (1ll << 32);
   if (fast) return launch_stream(a, s);
   const int G = q_heads / kv_heads;
   const size_t smem = sizeof(float) * ((size_t)G * head_dim + (size_t)G * top_k + 2 * (size_t)G);
