@@ -213,6 +213,29 @@ int qq_sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, 
                                void* out, int64_t out_stride, uint32_t* err, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* The same attention with no workspace argument; it allocates nothing.  No
+ * reference counterpart: the reference gets its attention scratch from
+ * torch on every call.  This entry exists for callers that cannot allocate
+ * device memory at call time — an engine that reserves all memory before it
+ * serves and forbids allocations on its decode path, or a host program that
+ * binds this C-ABI without a device allocator of its own.  Its scratch is a
+ * fixed array inside the library (9,867,264 bytes per device: arrival
+ * counters for QQ_NOALLOC_MAX_BS requests and partial records for a grid of
+ * at most 148 blocks).  Fast-path geometry only (bf16, 32 query heads over
+ * 4 KV heads, head_dim 128, top_k a multiple of 16, 16-byte aligned rows
+ * and pools) and bs <= QQ_NOALLOC_MAX_BS; anything else returns
+ * QQ_ERR_UNSUPPORTED.  The first call on a device, made with that device
+ * current, does the set-up (looks up the array's address, sets the kernel's
+ * shared-memory limit) and must come before any stream capture.  Every call
+ * clears the counters it uses on `stream` first.  Calls that overlap on one
+ * device share the array and race: keep them on one stream. */
+#define QQ_NOALLOC_MAX_BS 1024
+int qq_sparse_decode_attention_noalloc(const qq_batch* batch, int top_k, const void* q, int dtype,
+                                       int q_heads, int kv_heads, int head_dim, int64_t q_stride,
+                                       const int32_t* rows, const void* k_pool, const void* v_pool,
+                                       int64_t kv_row_stride, int64_t num_rows, float scaling,
+                                       void* out, int64_t out_stride, uint32_t* err, void* stream);
+
 /* ---- [H3] HiSparse swap-in -------------------------------------------- */
 /* For every request of the batch: fast path (seq_len <= buf: row = slot =
  * position) or first-occurrence dedupe, hit detection in LRU order,

@@ -34,6 +34,7 @@ QQ_STEP_FINALIZE = 2
 
 QQ_MAX_LAYERS = 128
 QQ_MAX_BS = 4096
+QQ_NOALLOC_MAX_BS = 1024
 
 
 class QQQuestState(ctypes.Structure):
@@ -120,6 +121,9 @@ SIGNATURES: dict[str, tuple] = {
     "qq_sparse_decode_attention": (
         c_int, [_B, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p,
                 c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "qq_sparse_decode_attention_noalloc": (
+        c_int, [_B, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p,
+                c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
     "qq_hisparse_swap_in": (
         c_int, [_H, c_int, _B, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
                 c_void_p]),

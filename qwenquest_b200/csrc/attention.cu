@@ -30,6 +30,7 @@
 #include <cfloat>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -722,5 +723,126 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
       return QQ_ERR_CUDA;
     attn_generic_kernel<float><<<grid, 128, smem, s>>>(a, q_heads, kv_heads, head_dim);
   }
+  return launch_status();
+}
+
+// ------------------------------------------------------------------ attention without a workspace
+//
+// Some callers cannot hand the library a workspace: an engine that reserves
+// all device memory for its KV pool and activation arena before serving and
+// allows no allocation on the decode path (an allocation there can block on
+// the device or fragment the reserved region), or a host program that binds
+// this C-ABI directly (cgo, JNI, ctypes) and has no device allocator of its
+// own.  qq_sparse_decode_attention_noalloc serves them: the streaming
+// kernel's scratch (arrival counters and split partials) lives in one
+// fixed-size array compiled into this library, so a call allocates nothing.
+//
+// * Limits: at most QQ_NOALLOC_MAX_BS requests and the fast-path geometry
+//   only (bf16, 32 query heads over 4 KV heads, head_dim 128, top_k a
+//   multiple of 16); anything else returns QQ_ERR_UNSUPPORTED.  The grid is
+//   capped at kNoAllocBlocks blocks, the number of blocks the partial
+//   records are sized for.
+// * Set-up: the first call on each device, made with that device current,
+//   looks up the array's device address (cudaGetSymbolAddress) and sets the
+//   kernel's shared-memory limit.  Make that first call before any stream
+//   capture begins.
+// * Each call clears the arrival counters it uses (an async memset on the
+//   caller's stream) before the kernel runs; the partial records need no
+//   clearing.
+// * One array per device: calls that overlap on the same device (two
+//   streams, or two host threads, with both kernels in flight) race on it
+//   and give wrong results.  Order them on one stream.
+
+namespace qq {
+
+constexpr int kNoAllocBlocks = 148;
+constexpr int kNoAllocWarps = 8;  // warps per block of the instantiation below
+constexpr int kNoAllocSlots = 3;
+constexpr size_t kNoAllocCounterBytes = sizeof(int32_t) * kKV * QQ_NOALLOC_MAX_BS;
+constexpr size_t kNoAllocPartialBytes =
+    sizeof(float) * (size_t)kNoAllocBlocks * kNoAllocWarps * 2 * kPartFloats;
+constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + kNoAllocPartialBytes;
+static_assert(kNoAllocCounterBytes % 256 == 0, "partials start 256-byte aligned");
+
+// 16 KiB of counters + 9.4 MiB of partial records (9,867,264 bytes).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kNoAllocMaxDevices];  // device address of the array, per device once set up
+
+// Device address of the scratch array on the current device; the first call
+// per device does the set-up.
+int noalloc_setup(void** scratch) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return QQ_ERR_CUDA;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return QQ_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return QQ_ERR_CUDA;
+    using Cfg = StreamCfg<kNoAllocWarps, kNoAllocSlots>;
+    if (cudaFuncSetAttribute(attn_stream_kernel<kNoAllocWarps, kNoAllocSlots>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem) != cudaSuccess)
+      return QQ_ERR_CUDA;
+    g_noalloc_ptr[dev] = p;
+  }
+  *scratch = g_noalloc_ptr[dev];
+  return QQ_OK;
+}
+
+}  // namespace
+}  // namespace qq
+
+extern "C" int qq_sparse_decode_attention_noalloc(const qq_batch* batch, int top_k, const void* q, int dtype,
+                                                  int q_heads, int kv_heads, int head_dim, int64_t q_stride,
+                                                  const int32_t* rows, const void* k_pool, const void* v_pool,
+                                                  int64_t kv_row_stride, int64_t num_rows, float scaling,
+                                                  void* out, int64_t out_stride, uint32_t* err, void* stream) {
+  if (batch == nullptr || q == nullptr || rows == nullptr || k_pool == nullptr || v_pool == nullptr ||
+      out == nullptr || top_k <= 0 || kv_heads <= 0 || head_dim <= 0 || q_heads % kv_heads != 0 ||
+      num_rows <= 0)
+    return QQ_ERR_INVALID;
+  if (batch->bs == 0) return QQ_OK;
+  if (batch->bs < 0 || batch->seq_lens == nullptr) return QQ_ERR_INVALID;
+  if (batch->bs > QQ_NOALLOC_MAX_BS) return QQ_ERR_UNSUPPORTED;
+  const int64_t row_bytes = kv_row_stride * 2;
+  const bool geometry = dtype == QQ_BF16 && kv_heads == kKV && head_dim == kD && q_heads == kH &&
+                        top_k % kToks == 0 && (int64_t)batch->bs * top_k * kKV < (1ll << 31) &&
+                        row_bytes > 0 && row_bytes % 16 == 0 && row_bytes < (1ll << 32) &&
+                        (reinterpret_cast<uintptr_t>(k_pool) % 16) == 0 &&
+                        (reinterpret_cast<uintptr_t>(v_pool) % 16) == 0 &&
+                        (reinterpret_cast<uintptr_t>(rows) % 16) == 0 && (q_stride % 2) == 0 &&
+                        (out_stride % 2) == 0 && (reinterpret_cast<uintptr_t>(out) % 4) == 0;
+  if (!geometry) return QQ_ERR_UNSUPPORTED;
+  void* scratch = nullptr;
+  const int rc = noalloc_setup(&scratch);
+  if (rc != QQ_OK) return rc;
+  cudaStream_t s = as_stream(stream);
+  if (cudaMemsetAsync(scratch, 0, sizeof(int32_t) * kKV * (size_t)batch->bs, s) != cudaSuccess)
+    return QQ_ERR_CUDA;
+  AttnArgs a{};
+  a.seq_lens = batch->seq_lens;
+  a.bs = batch->bs;
+  a.top_k = top_k;
+  a.q = q;
+  a.q_stride = q_stride;
+  a.rows = rows;
+  a.k_pool = static_cast<const char*>(k_pool);
+  a.v_pool = static_cast<const char*>(v_pool);
+  a.row_stride_bytes = row_bytes;
+  a.num_rows = num_rows;
+  a.scaling = scaling;
+  a.scale_log2 = scaling * 1.4426950408889634f;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.err = err;
+  a.seg_count = static_cast<int32_t*>(scratch);
+  a.part = reinterpret_cast<float*>(static_cast<char*>(scratch) + kNoAllocCounterBytes);
+  using Cfg = StreamCfg<kNoAllocWarps, kNoAllocSlots>;
+  const int blocks = sm_count() < kNoAllocBlocks ? sm_count() : kNoAllocBlocks;
+  attn_stream_kernel<kNoAllocWarps, kNoAllocSlots><<<blocks, Cfg::kThreads, Cfg::kSmem, s>>>(a);
   return launch_status();
 }
