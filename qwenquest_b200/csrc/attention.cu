@@ -111,21 +111,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 16-byte async copy global -> shared (L2 only).
-__device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* gmem_src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gmem_src) : "memory");
-}
-// The same with a source size: the bytes past src_bytes (all 16 for 0) are written as zeros.
-__device__ __forceinline__ void cp_async_16_zfill(uint32_t smem_dst, const void* gmem_src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_dst), "l"(gmem_src), "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 #define kNegInf (-__int_as_float(0x7f800000))
 
 // ------------------------------------------------------------------ stream-K walk

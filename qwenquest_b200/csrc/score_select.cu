@@ -1,24 +1,32 @@
 // [Q5][Q6][Q7] Quest page scoring, top-k page selection and the position
 // layout, fused into one launch per layer.
 //
-// Grid (page chunk, request).  Each block averages the request's GQA query
-// groups into q̄ (shared memory), then every warp scores whole pages: a page's
-// bounds are 4*nch bytes (2 KiB at 4 KV heads x 128 channels) read as
-// coalesced 128-bit loads, lane l taking 16-byte words l, l+32, ... so that
-// its q̄ values stay in registers.  The last block of a request to finish (an
-// arrival counter in the workspace) selects the top pages from the fp32 scores
-// (L2-resident by then) and writes the position layout, the req_to_token
-// translation and actual_lens.  Scoring is HBM-bound; selection is a short
-// latency-bound tail that overlaps other requests' scoring.
+// Persistent: one 512-thread block per SM (at most), walking work units with
+// a stride of the grid.  A unit is one part of one request's pages: with a
+// small batch a request is split into `parts` page ranges so that every SM
+// streams bounds.  Within a unit each warp streams its own pages (page
+// pg0 + warp + 16 m) straight into registers: lane l takes 16-byte words
+// l, l + 32, ... of a page (four channels' (min, max) pairs each) so that
+// its q̄ values stay in registers, the sign of q̄ picks max or min by a byte
+// permute, and DEPTH pages per warp are in flight while the warp reduces an
+// earlier one.  There is no block barrier inside a unit: the only ones are
+// around q̄ (computed once per unit, while the first pages are in flight)
+// and the unit's end, where the block arrives on the request's counter in
+// the workspace.  The last part of a request to arrive selects the top pages
+// from the fp32 scores (L2-resident by then): an 8-bit-per-pass radix
+// select of the sel-th largest score, ties to the lower pages, a rank sort of
+// the selected pages, then the position layout with the req_to_token reads
+// in flight together.
+
+#include <type_traits>
 
 #include "common.cuh"
 
 namespace qq {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kPagesPerBlock = 64;
 
 struct SelectArgs {
   qq_quest_state st;
@@ -46,139 +54,43 @@ struct SelectArgs {
   int64_t nt_buf;
   int64_t nt_dst_num_rows;
   int32_t* counters;
+  int pages;      // page slots per request covered by the parts (max_pages, or num_pages)
+  int parts;      // units per request: part j takes pages [j * pages / parts, (j + 1) * pages / parts)
+  int units;      // bs * parts
   int score_all;  // page_scores API: score pages [0, num_pages) of every request, no selection
   int num_pages;
 };
 
-__device__ __forceinline__ float bound_term(uint32_t pair, float q) {
-  // pair: low half = min, high half = max (bf16); where(q >= 0, max, min)
-  const float b = q >= 0.f ? __uint_as_float(pair & 0xFFFF0000u) : __uint_as_float(pair << 16);
-  return __fmul_rn(q, b);
+// Dynamic shared memory of the selection: order keys of the candidate
+// pages, then the selected pages, their keys and their score order.
+inline size_t selection_smem(int max_pages, int sel) {
+  return sizeof(uint32_t) * (size_t)max_pages +
+         (sizeof(uint64_t) + 2 * sizeof(int32_t)) * (size_t)(sel > 0 ? sel : 0) + 16;
 }
 
-__device__ __forceinline__ uint64_t composite(float score, uint32_t page) {
-  return ((uint64_t)float_order_key(score) << 32) | (uint64_t)(0xFFFFFFFFu - page);
+__device__ __forceinline__ uint32_t lane_mask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
 }
 
-template <typename QT, int KITER>
-__global__ void __launch_bounds__(kThreads) score_select_kernel(SelectArgs a) {
-  __shared__ float s_qbar[QQ_MAX_CHANNELS];
-  __shared__ uint64_t s_gm[64];
-  __shared__ uint64_t s_T;
-  __shared__ int s_M;
-  __shared__ int s_last;
-  extern __shared__ uint64_t s_dyn[];  // [max_pages] candidates, then [sel] selected pages
+// q * bound + acc: for a bf16 query mean the product of two bf16 values is
+// exact in fp32, so one fused multiply-add rounds exactly like the
+// reference's product-then-sum; an fp32 mean keeps the separate rounding.
+template <typename QT>
+__device__ __forceinline__ float bound_fma(float q, float b, float acc) {
+  if constexpr (std::is_same<QT, float>::value) return __fadd_rn(acc, __fmul_rn(q, b));
+  else return __fmaf_rn(q, b, acc);
+}
 
+// The request's selection and position layout, by the whole block.
+__device__ void select_request(const SelectArgs& a, int i, int64_t req, int64_t L, int64_t C, bool is_long,
+                               unsigned char* smem, int* s_hist, int& s_digit, int& s_above, int& s_ngt) {
   const qq_quest_state& st = a.st;
-  const int i = blockIdx.y;
-  const int chunk = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t req = a.reqs[i];
   const int P = st.page_size;
-  const int nch = st.kv_heads * st.head_dim;
-  const int64_t L = a.score_all ? 0 : a.seq_lens[i];
-
-  int64_t F, C;
-  bool is_long;
-  if (a.score_all) {
-    F = C = a.num_pages;
-    is_long = true;
-  } else {
-    F = L / P;
-    if (F > st.max_pages) F = st.max_pages;  // seq_len beyond max_context_len: never index past the slot
-    C = st.avoid_recent_overlap ? (F > 0 ? F - 1 : 0) : F;
-    is_long = L > st.top_k;
-  }
-
-  // (a) the new token's K/V into its pool row (quest_only.py:136-137, coordinator.py:226-228)
-  if (a.nt_k != nullptr && chunk == 0) {
-    const int64_t buf = a.nt_buf;
-    const int64_t dst = a.nt_dst_rows != nullptr ? a.nt_dst_rows[i]
-                                                 : req * (buf + 1) + (L - 1 < buf ? L - 1 : buf);
-    for (int w = tid; dst >= 0 && dst < a.nt_dst_num_rows && w < a.nt_row_words; w += kThreads) {
-      a.nt_k_dst[dst * a.nt_dst_stride_words + w] = a.nt_k[i * a.nt_src_stride_words + w];
-      a.nt_v_dst[dst * a.nt_dst_stride_words + w] = a.nt_v[i * a.nt_src_stride_words + w];
-    }
-  }
-
-  // (b) scores of candidate pages [p0, p1)
-  const int64_t p0 = (int64_t)chunk * kPagesPerBlock;
-  const int64_t p1 = min(C, p0 + kPagesPerBlock);
-  float* scores = a.scores + (int64_t)i * st.max_pages;
-  if (is_long && p0 < p1) {
-    const QT* q = static_cast<const QT*>(a.q) + (int64_t)i * a.q_stride;
-    const int G = a.q_heads / st.kv_heads;
-    const int D = st.head_dim;
-    for (int c = tid; c < nch; c += kThreads) {
-      const int h = c / D, d = c - h * D;
-      float acc = 0.f;
-      for (int g = 0; g < G; ++g) acc = __fadd_rn(acc, Elem<QT>::load(q + (int64_t)(h * G + g) * D + d));
-      // mean in the query dtype (quest.py:390): fp32 sum / G rounded to QT
-      s_qbar[c] = G == 1 ? acc : Elem<QT>::round(__fdiv_rn(acc, (float)G));
-    }
-    __syncthreads();
-    float qv[KITER][4];
-    const int nvec = nch >> 2;
-#pragma unroll
-    for (int it = 0; it < KITER; ++it) {
-      const int j = lane + 32 * it;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) qv[it][e] = j < nvec ? s_qbar[4 * j + e] : 0.f;
-    }
-    const uint16_t* breq = st.page_bounds +
-                           (((size_t)a.layer * st.max_reqs + req) * st.max_pages) * (size_t)nch * 2;
-    // two pages per warp iteration: 2 * KITER independent 128-bit loads in flight per lane
-    for (int64_t p = p0 + warp; p < p1; p += 2 * kWarps) {
-      const int64_t pp[2] = {p, p + kWarps};
-      uint4 w[2][KITER];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const uint4* pb = reinterpret_cast<const uint4*>(breq + (size_t)pp[u] * nch * 2);
-#pragma unroll
-        for (int it = 0; it < KITER; ++it) {
-          const int j = lane + 32 * it;
-          w[u][it] = (j < nvec && pp[u] < p1) ? ld_stream_u4(pb + j) : make_uint4(0, 0, 0, 0);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float acc = 0.f;
-#pragma unroll
-        for (int it = 0; it < KITER; ++it) {
-          if (lane + 32 * it < nvec) {
-            acc = __fadd_rn(acc, bound_term(w[u][it].x, qv[it][0]));
-            acc = __fadd_rn(acc, bound_term(w[u][it].y, qv[it][1]));
-            acc = __fadd_rn(acc, bound_term(w[u][it].z, qv[it][2]));
-            acc = __fadd_rn(acc, bound_term(w[u][it].w, qv[it][3]));
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-        if (lane == 0 && pp[u] < p1) scores[pp[u]] = acc;
-      }
-    }
-  }
-  if (a.score_all) return;
-  // pages that are complete but not candidates read -inf (quest.py:450-451)
-  if (is_long) {
-    const int64_t m0 = max(p0, C), m1 = min(F, p0 + kPagesPerBlock);
-    for (int64_t p = m0 + tid; p < m1; p += kThreads) scores[p] = -__int_as_float(0x7f800000);
-  }
-
-  // (c) the last block of this request does the selection; every writer
-  // fences before the arrival so that block sees all scores
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int old = atomicAdd(&a.counters[i], 1);
-    s_last = old == (int)gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (tid == 0) a.counters[i] = 0;
-
   const int top_k = st.top_k;
+  const float* scores = a.scores + (int64_t)i * st.max_pages;
   const int n = (int)(L < top_k ? L : top_k);
   if (a.actual_lens != nullptr && tid == 0) a.actual_lens[i] = n;
   int32_t* pos_out = a.positions + (int64_t)i * top_k;
@@ -186,70 +98,276 @@ __global__ void __launch_bounds__(kThreads) score_select_kernel(SelectArgs a) {
   const int32_t* r2t = a.r2t != nullptr ? a.r2t + req * a.r2t_stride : nullptr;
   const int64_t last = L > 0 ? L - 1 : 0;
 
-  if (!is_long) {  // dense: 0 .. L-1, padded with L-1 (quest.py:339-340)
-    for (int s = tid; s < top_k; s += kThreads) {
-      const int32_t pos = (int32_t)(s < last ? s : last);
-      pos_out[s] = pos;
-      if (rows_out != nullptr && s < n) rows_out[s] = pos < a.r2t_stride ? r2t[pos] : 0;
-    }
-    return;
-  }
+  const int sel_req = top_k / P - 1;
+  const int sel = is_long ? (int)min((int64_t)sel_req, C) : 0;
+  uint32_t* s_okey = reinterpret_cast<uint32_t*>(smem);
+  int32_t* s_selp = reinterpret_cast<int32_t*>(s_okey + st.max_pages);
+  uint64_t* s_selk = reinterpret_cast<uint64_t*>(
+      reinterpret_cast<uintptr_t>(s_selp + (sel_req > 0 ? sel_req : 0) + 1) & ~(uintptr_t)7);
+  int32_t* s_order = reinterpret_cast<int32_t*>(s_selk + (sel_req > 0 ? sel_req : 0));
 
-  const int sel = top_k / P - 1;
-  uint64_t* s_cand = s_dyn;
-  int32_t* s_sel = reinterpret_cast<int32_t*>(s_dyn + st.max_pages);
   if (sel > 0) {
-    // threshold: the sel-th largest of 64 group maxima bounds the sel-th largest score
-    uint64_t T = 0;
-    if (sel <= 64) {
-      uint64_t m = 0;
-      for (int64_t p = tid; p < C; p += kThreads) m = max(m, composite(__ldcg(scores + p), (uint32_t)p));
-      m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
-      m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
-      if ((tid & 3) == 0) s_gm[tid >> 2] = m;
+    for (int64_t p = tid; p < C; p += kThreads) s_okey[p] = float_order_key(__ldcg(scores + p));
+    // radix select, 8 bits a pass from the top: t = the sel-th largest order
+    // key, `above` = keys greater than t
+    uint32_t prefix = 0, mask = 0;
+    int k = sel, above = 0;
+    const int64_t c_round = (C + 31) / 32 * 32;  // whole warps for __match_any_sync
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      if (tid < 256) s_hist[tid] = 0;
       __syncthreads();
-      if (tid < 64) {
-        const uint64_t me = s_gm[tid];
-        int rank = 0;
-        for (int j = 0; j < 64; ++j) {
-          const uint64_t o = s_gm[j];
-          rank += (o > me) || (o == me && j < tid);
-        }
-        if (rank == sel - 1) s_T = me;
+      for (int64_t p = tid; p < c_round; p += kThreads) {
+        const bool in = p < C && (s_okey[p] & mask) == prefix;
+        const uint32_t digit = in ? (s_okey[p] >> shift) & 255u : 256u;
+        const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+        if (in && (__ffs(peers) - 1) == lane) atomicAdd(&s_hist[digit], __popc(peers));
       }
       __syncthreads();
-      T = s_T;
+      if (warp == 0) {
+        int c8[8], tot = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          c8[e] = s_hist[255 - 8 * lane - e];
+          tot += c8[e];
+        }
+        int incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        int run = incl - tot;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (run < k && k <= run + c8[e]) {
+            s_digit = 255 - 8 * lane - e;
+            s_above = run;
+          }
+          run += c8[e];
+        }
+      }
+      __syncthreads();
+      prefix |= (uint32_t)s_digit << shift;
+      mask |= 255u << shift;
+      above += s_above;
+      k -= s_above;
     }
-    if (tid == 0) s_M = 0;
+    // selected: every key above t, and the k lowest pages among keys equal to t
+    if (tid == 0) s_ngt = 0;
     __syncthreads();
-    for (int64_t p = tid; p < C; p += kThreads) {
-      const uint64_t key = composite(__ldcg(scores + p), (uint32_t)p);
-      if (key >= T) s_cand[atomicAdd(&s_M, 1)] = key;
+    for (int64_t p = tid; p < C; p += kThreads)
+      if (s_okey[p] > prefix) s_selp[atomicAdd(&s_ngt, 1)] = (int32_t)p;
+    if (warp == kWarps - 1) {
+      int taken = 0;
+      for (int64_t b = 0; b < C && taken < k; b += 32) {
+        const int64_t p = b + lane;
+        const bool eq = p < C && s_okey[p] == prefix;
+        const uint32_t bal = __ballot_sync(0xffffffffu, eq);
+        const int r = taken + __popc(bal & lane_mask_lt());
+        if (eq && r < k) s_selp[above + r] = (int32_t)p;
+        taken += __popc(bal);
+      }
     }
     __syncthreads();
-    const int M = s_M;
-    for (int c = tid; c < M; c += kThreads) {
-      const uint64_t kc = s_cand[c];
+    // descending score, ties -> lower page (quest.py:452 topk order, stable)
+    for (int c = tid; c < sel; c += kThreads) {
+      const int32_t p = s_selp[c];
+      s_selk[c] = ((uint64_t)s_okey[p] << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)p);
+    }
+    __syncthreads();
+    for (int c = tid; c < sel; c += kThreads) {
+      const uint64_t kc = s_selk[c];
       int rank = 0;
-      for (int j = 0; j < M; ++j) rank += s_cand[j] > kc;
-      if (rank < sel) s_sel[rank] = (int32_t)(0xFFFFFFFFu - (uint32_t)(kc & 0xFFFFFFFFu));
+#pragma unroll 8
+      for (int j = 0; j < sel; ++j) rank += s_selk[j] > kc;
+      s_order[rank] = s_selp[c];
     }
     __syncthreads();
   }
-  // layout: selected pages in score order, then the recent window (quest.py:453-459)
+  // layout: selected pages in score order, then the recent window
+  // (quest.py:453-459); dense 0 .. L-1 padded with L-1 (quest.py:339-340).
+  // Four positions per thread in flight so the req_to_token reads overlap.
   const int64_t rp0 = L - P > 0 ? L - P : 0;
-  const int sp = sel * P;
-  for (int s = tid; s < top_k; s += kThreads) {
-    int64_t pos;
-    if (s < sp) {
-      const int b = s / P;
-      pos = (int64_t)s_sel[b] * P + (s - b * P);
-    } else {
-      const int64_t r = rp0 + (s - sp);
-      pos = r < last ? r : last;
+  const int sp = sel_req * P;
+  constexpr int kU = 4;
+  for (int s0 = 0; s0 < top_k; s0 += kThreads * kU) {
+    int64_t pos[kU];
+    int32_t rv[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int s = s0 + u * kThreads + tid;
+      if (!is_long) {
+        pos[u] = s < last ? s : last;
+      } else if (s < sp) {
+        const int b = s / P;
+        const int32_t page = b < sel ? s_order[b] : (sel > 0 ? s_order[sel - 1] : 0);
+        pos[u] = (int64_t)page * P + (s - b * P);
+      } else {
+        const int64_t r = rp0 + (s - sp);
+        pos[u] = r < last ? r : last;
+      }
     }
-    pos_out[s] = (int32_t)pos;
-    if (rows_out != nullptr) rows_out[s] = pos < a.r2t_stride ? r2t[pos] : 0;
+    if (rows_out != nullptr) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int s = s0 + u * kThreads + tid;
+        rv[u] = (s < top_k && (is_long || s < n) && pos[u] < a.r2t_stride) ? __ldg(r2t + pos[u]) : 0;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int s = s0 + u * kThreads + tid;
+      if (s < top_k) {
+        pos_out[s] = (int32_t)pos[u];
+        if (rows_out != nullptr && (is_long || s < n)) rows_out[s] = rv[u];
+      }
+    }
+  }
+}
+
+// KW 16-byte words per lane and page, DEPTH pages in flight per warp.
+template <typename QT, int KW, int DEPTH>
+__global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a) {
+  __shared__ float s_qbar[QQ_MAX_CHANNELS];
+  __shared__ int s_hist[256];
+  __shared__ int s_digit, s_above, s_last, s_ngt;
+  extern __shared__ __align__(16) unsigned char s_dyn[];  // the selection's keys and pages
+
+  const qq_quest_state& st = a.st;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nch = st.kv_heads * st.head_dim;
+  const int nvec = nch >> 2;
+  const size_t page_words = (size_t)nvec;  // 16-byte words per page
+
+  for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+    const int i = u / a.parts, j = u - (u / a.parts) * a.parts;
+    const int64_t req = a.reqs[i];
+    const int64_t L = a.score_all ? 0 : a.seq_lens[i];
+    int64_t F, C;
+    bool is_long;
+    if (a.score_all) {
+      F = C = a.num_pages;
+      is_long = true;
+    } else {
+      F = L / st.page_size;
+      if (F > st.max_pages) F = st.max_pages;  // seq_len beyond max_context_len: never index past the slot
+      C = st.avoid_recent_overlap ? (F > 0 ? F - 1 : 0) : F;
+      is_long = L > st.top_k;
+    }
+    const int64_t pg0 = (int64_t)j * a.pages / a.parts, pg1 = (int64_t)(j + 1) * a.pages / a.parts;
+    const int64_t p_end = is_long ? min(pg1, C) : pg0;  // candidate pages of this part: [pg0, p_end)
+    float* scores = a.scores + (int64_t)i * st.max_pages;
+    const uint4* bounds = reinterpret_cast<const uint4*>(st.page_bounds) +
+                          ((size_t)a.layer * st.max_reqs + req) * st.max_pages * page_words;
+
+    // the first DEPTH pages of this warp in flight before anything else
+    uint4 buf[DEPTH][KW];
+    auto load_page = [&](uint4 (&w)[KW], int64_t p) {
+      const uint4* src = bounds + (size_t)p * page_words;
+#pragma unroll
+      for (int it = 0; it < KW; ++it) {
+        const int wi = lane + 32 * it;
+        w[it] = wi < nvec ? ld_stream_u4(src + wi) : make_uint4(0, 0, 0, 0);
+      }
+    };
+    const int64_t pw0 = pg0 + warp;
+#pragma unroll
+    for (int d = 0; d < DEPTH; ++d)
+      if (pw0 + d * kWarps < p_end) load_page(buf[d], pw0 + d * kWarps);
+
+    // (a) the new token's K/V into its pool row (quest_only.py:136-137, coordinator.py:226-228)
+    if (a.nt_k != nullptr && j == 0) {
+      const int64_t b = a.nt_buf;
+      const int64_t dst = a.nt_dst_rows != nullptr ? a.nt_dst_rows[i] : req * (b + 1) + (L - 1 < b ? L - 1 : b);
+      for (int w = tid; dst >= 0 && dst < a.nt_dst_num_rows && w < a.nt_row_words; w += kThreads) {
+        a.nt_k_dst[dst * a.nt_dst_stride_words + w] = a.nt_k[i * a.nt_src_stride_words + w];
+        a.nt_v_dst[dst * a.nt_dst_stride_words + w] = a.nt_v[i * a.nt_src_stride_words + w];
+      }
+    }
+
+    // (b) scores of the part's candidate pages
+    if (pg0 < p_end) {
+      // q̄: the GQA mean in the query dtype (quest.py:390), fp32 sum over the
+      // group in head order, eight loads in flight at a time
+      const QT* q = static_cast<const QT*>(a.q) + (int64_t)i * a.q_stride;
+      const int G = a.q_heads / st.kv_heads;
+      const int D = st.head_dim;
+      for (int c = tid; c < nch; c += kThreads) {
+        const int h = c / D, d = c - h * D;
+        const QT* qc = q + (int64_t)h * G * D + d;
+        float acc = 0.f;
+        int g = 0;
+        for (; g + 8 <= G; g += 8) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = Elem<QT>::load(qc + (int64_t)(g + e) * D);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, v[e]);
+        }
+        for (; g < G; ++g) acc = __fadd_rn(acc, Elem<QT>::load(qc + (int64_t)g * D));
+        s_qbar[c] = G == 1 ? acc : Elem<QT>::round(__fdiv_rn(acc, (float)G));
+      }
+      __syncthreads();
+      float qv[KW][4];
+      uint32_t pick[KW][4];
+#pragma unroll
+      for (int it = 0; it < KW; ++it) {
+        const int wi = lane + 32 * it;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          qv[it][e] = wi < nvec ? s_qbar[4 * wi + e] : 0.f;
+          pick[it][e] = qv[it][e] >= 0.f ? 0x3244u : 0x1044u;  // high half (max) or low half (min)
+        }
+      }
+      for (int64_t pc = pw0; pc < p_end; pc += DEPTH * kWarps) {
+#pragma unroll
+        for (int d = 0; d < DEPTH; ++d) {
+          const int64_t p = pc + d * kWarps;
+          if (p < p_end) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int it = 0; it < KW; ++it) {
+              const uint4 w = buf[d][it];
+              acc[0] = bound_fma<QT>(qv[it][0], __uint_as_float(__byte_perm(w.x, 0u, pick[it][0])), acc[0]);
+              acc[1] = bound_fma<QT>(qv[it][1], __uint_as_float(__byte_perm(w.y, 0u, pick[it][1])), acc[1]);
+              acc[2] = bound_fma<QT>(qv[it][2], __uint_as_float(__byte_perm(w.z, 0u, pick[it][2])), acc[2]);
+              acc[3] = bound_fma<QT>(qv[it][3], __uint_as_float(__byte_perm(w.w, 0u, pick[it][3])), acc[3]);
+            }
+            // the next page of this slot goes in flight before the reduction
+            const int64_t pn = p + DEPTH * kWarps;
+            if (pn < p_end) load_page(buf[d], pn);
+            float sum = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+            if (lane == 0) scores[p] = sum;
+          }
+        }
+      }
+    }
+    if (a.score_all) continue;
+    // pages that are complete but not candidates read -inf (quest.py:450-451)
+    if (is_long) {
+      const int64_t m0 = max(pg0, C), m1 = min(F, pg1);
+      for (int64_t p = m0 + tid; p < m1; p += kThreads) scores[p] = -__int_as_float(0x7f800000);
+    }
+
+    // (c) the block arrives on the request's counter; the last part to
+    // arrive does the selection.  The barrier and thread 0's fence order
+    // every thread's score writes before the arrival, and the last arriver's
+    // fence orders its reads after it.
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      const bool last = atomicAdd(&a.counters[i], 1) == a.parts - 1;
+      if (last) {
+        __threadfence();
+        a.counters[i] = 0;
+      }
+      s_last = last;
+    }
+    __syncthreads();
+    if (s_last) select_request(a, i, req, L, C, is_long, s_dyn, s_hist, s_digit, s_above, s_ngt);
+    __syncthreads();  // the selection's shared memory is free again
   }
 }
 
@@ -267,51 +385,72 @@ __global__ void group_queries_kernel(const QT* __restrict__ q, int q_heads, int 
   }
 }
 
-template <typename QT>
-int launch_select(const SelectArgs& a, dim3 grid, size_t smem, int kiter, cudaStream_t s) {
-  switch (kiter) {
-    case 1:
-      score_select_kernel<QT, 1><<<grid, kThreads, smem, s>>>(a);
-      break;
-    case 2:
-      score_select_kernel<QT, 2><<<grid, kThreads, smem, s>>>(a);
-      break;
-    case 4:
-      score_select_kernel<QT, 4><<<grid, kThreads, smem, s>>>(a);
-      break;
-    case 8:
-      score_select_kernel<QT, 8><<<grid, kThreads, smem, s>>>(a);
-      break;
-    default:
-      return QQ_ERR_UNSUPPORTED;
-  }
-  return launch_status();
+// Words per lane for nch channels (nch / 4 16-byte words per page).
+int words_for(int nch) {
+  const int nvec = nch / 4;
+  return nvec <= 32 ? 1 : nvec <= 64 ? 2 : nvec <= 128 ? 4 : 8;  // nch <= QQ_MAX_CHANNELS = 1024
 }
 
-int kiter_for(int nch) {
-  const int k = (nch + 127) / 128;
-  return k <= 1 ? 1 : k <= 2 ? 2 : k <= 4 ? 4 : 8;
+template <typename QT>
+const void* kernel_for(int kw) {
+  switch (kw) {
+    case 1: return (const void*)score_select_kernel<QT, 1, 4>;
+    case 2: return (const void*)score_select_kernel<QT, 2, 4>;
+    case 4: return (const void*)score_select_kernel<QT, 4, 3>;
+    default: return (const void*)score_select_kernel<QT, 8, 1>;
+  }
+}
+
+template <typename QT>
+int launch_select(const SelectArgs& a, int grid, int kw, size_t smem, cudaStream_t s) {
+  static size_t attr_smem = 48 * 1024;  // the default limit
+  if (smem > attr_smem) {
+    const int kws[4] = {1, 2, 4, 8};
+    for (int k : kws)
+      if (cudaFuncSetAttribute(kernel_for<QT>(k), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+        return QQ_ERR_CUDA;
+    attr_smem = smem;
+  }
+  switch (kw) {
+    case 1: score_select_kernel<QT, 1, 4><<<grid, kThreads, smem, s>>>(a); break;
+    case 2: score_select_kernel<QT, 2, 4><<<grid, kThreads, smem, s>>>(a); break;
+    case 4: score_select_kernel<QT, 4, 3><<<grid, kThreads, smem, s>>>(a); break;
+    default: score_select_kernel<QT, 8, 1><<<grid, kThreads, smem, s>>>(a); break;
+  }
+  return launch_status();
 }
 
 bool valid_state(const qq_quest_state* st) {
   return st != nullptr && st->page_bounds && st->num_layers > 0 && st->max_reqs > 0 &&
          st->max_pages > 0 && st->kv_heads > 0 && st->head_dim > 0 && st->page_size > 0 &&
-         st->kv_heads * st->head_dim <= QQ_MAX_CHANNELS && (st->kv_heads * st->head_dim) % 4 == 0;
+         st->kv_heads * st->head_dim <= QQ_MAX_CHANNELS && (st->kv_heads * st->head_dim) % 4 == 0 &&
+         reinterpret_cast<uintptr_t>(st->page_bounds) % 16 == 0;
 }
 
-size_t select_smem(const qq_quest_state* st) {
-  const int sel = st->top_k / st->page_size;
-  return sizeof(uint64_t) * (size_t)st->max_pages + sizeof(int32_t) * (size_t)sel;
+int g_sm_count = 0;
+int sm_count() {
+  if (g_sm_count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (g_sm_count <= 0) g_sm_count = 148;
+  }
+  return g_sm_count;
 }
 
-template <typename QT>
-int set_smem_attr(size_t smem) {
-  const void* fns[4] = {(const void*)score_select_kernel<QT, 1>, (const void*)score_select_kernel<QT, 2>,
-                        (const void*)score_select_kernel<QT, 4>, (const void*)score_select_kernel<QT, 8>};
-  for (const void* f : fns)
-    if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return QQ_ERR_CUDA;
-  return QQ_OK;
+// Units and grid of one launch over `pages` page slots per request: with a
+// small batch every request is split into parts so that each SM streams
+// bounds, and no block does two selections.
+void plan_units(SelectArgs& a, int pages, int bs, int* grid) {
+  int parts = sm_count() / (bs > 0 ? bs : 1);
+  const int max_parts = pages / (2 * kWarps);  // at least two pages per warp and part
+  if (parts > max_parts) parts = max_parts;
+  if (parts < 1) parts = 1;
+  a.pages = pages;
+  a.parts = parts;
+  a.units = parts * bs;
+  *grid = a.units < sm_count() ? a.units : sm_count();
 }
 
 }  // namespace
@@ -369,18 +508,14 @@ extern "C" int qq_quest_retrieve_topk(const qq_quest_state* st, int layer, const
     a.nt_buf = nt->device_buffer_size;
     a.nt_dst_num_rows = nt->dst_num_rows;
   }
-  const size_t smem = select_smem(st);
+  const size_t smem = selection_smem(st->max_pages, st->top_k / st->page_size - 1);
   if (smem > 200 * 1024) return QQ_ERR_UNSUPPORTED;
-  const int chunks = (st->max_pages + kPagesPerBlock - 1) / kPagesPerBlock;
-  dim3 grid(chunks, batch->bs);
+  int grid = 0;
+  plan_units(a, st->max_pages, batch->bs, &grid);
   cudaStream_t s = as_stream(stream);
-  const int kiter = kiter_for(st->kv_heads * st->head_dim);
-  if (q_dtype == QQ_BF16) {
-    if (smem > 48 * 1024 && set_smem_attr<__nv_bfloat16>(smem) != QQ_OK) return QQ_ERR_CUDA;
-    return launch_select<__nv_bfloat16>(a, grid, smem, kiter, s);
-  }
-  if (smem > 48 * 1024 && set_smem_attr<float>(smem) != QQ_OK) return QQ_ERR_CUDA;
-  return launch_select<float>(a, grid, smem, kiter, s);
+  const int kw = words_for(st->kv_heads * st->head_dim);
+  if (q_dtype == QQ_BF16) return launch_select<__nv_bfloat16>(a, grid, kw, smem, s);
+  return launch_select<float>(a, grid, kw, smem, s);
 }
 
 extern "C" int qq_quest_group_queries(const void* q, int dtype, int bs, int q_heads, int kv_heads,
@@ -410,6 +545,7 @@ extern "C" int qq_quest_page_scores(const qq_quest_state* st, int layer, const q
     return QQ_ERR_INVALID;
   if (batch->bs == 0 || num_pages == 0) return QQ_OK;
   if (batch->bs < 0 || batch->bs > QQ_MAX_BS || !batch->req_pool_indices) return QQ_ERR_INVALID;
+  if (q_dtype != QQ_BF16 && q_dtype != QQ_F32) return QQ_ERR_INVALID;
   SelectArgs a{};
   a.st = *st;
   a.layer = layer;
@@ -420,10 +556,10 @@ extern "C" int qq_quest_page_scores(const qq_quest_state* st, int layer, const q
   a.scores = scores;
   a.score_all = 1;
   a.num_pages = num_pages;
-  dim3 grid((num_pages + kPagesPerBlock - 1) / kPagesPerBlock, batch->bs);
-  const int kiter = kiter_for(st->kv_heads * st->head_dim);
+  int grid = 0;
+  plan_units(a, num_pages, batch->bs, &grid);
+  const int kw = words_for(st->kv_heads * st->head_dim);
   cudaStream_t s = as_stream(stream);
-  if (q_dtype == QQ_BF16) return launch_select<__nv_bfloat16>(a, grid, 0, kiter, s);
-  if (q_dtype == QQ_F32) return launch_select<float>(a, grid, 0, kiter, s);
-  return QQ_ERR_INVALID;
+  if (q_dtype == QQ_BF16) return launch_select<__nv_bfloat16>(a, grid, kw, 0, s);
+  return launch_select<float>(a, grid, kw, 0, s);
 }
