@@ -169,13 +169,21 @@ inline int launch_status() {
 
 // Workspace layout: arrival counters (int32, kept at zero between launches) —
 // QQ_MAX_BS for the selection, QQ_MAX_BS for the bounds step, 4 * QQ_MAX_BS
-// for the attention's (request, KV head) segments — then the attention partials.
+// for the attention's (request, KV head) segments — then the selection's
+// per-part top-32 lists (QQ_MAX_BS lists of 32 uint64 keys), then the
+// attention partials.
 constexpr size_t kCounterBytes = sizeof(int32_t) * QQ_MAX_BS;
 enum CounterSlot { kCounterSelect = 0, kCounterStep = 1, kCounterAttn = 2 };
 inline int32_t* ws_counters(void* ws, CounterSlot slot) {
   return reinterpret_cast<int32_t*>(static_cast<char*>(ws) + slot * kCounterBytes);
 }
-constexpr size_t kPartialOffset = 6 * kCounterBytes;
+constexpr size_t kSelectListOffset = 6 * kCounterBytes;
+constexpr int kSelectListLen = 32;
+constexpr size_t kSelectListBytes = sizeof(uint64_t) * kSelectListLen * QQ_MAX_BS;
+inline uint64_t* ws_select_lists(void* ws) {
+  return reinterpret_cast<uint64_t*>(static_cast<char*>(ws) + kSelectListOffset);
+}
+constexpr size_t kPartialOffset = kSelectListOffset + kSelectListBytes;
 
 // Attention partials: two (m, l, O) records of 8 query heads x 128 channels
 // per warp of the streaming grid (at most 16 warps per SM).

@@ -54,6 +54,7 @@ struct SelectArgs {
   int64_t nt_buf;
   int64_t nt_dst_num_rows;
   int32_t* counters;
+  uint64_t* lists;  // per-part top-32 lists (workspace)
   int pages;      // page slots per request covered by the parts (max_pages, or num_pages)
   int parts;      // units per request: part j takes pages [j * pages / parts, (j + 1) * pages / parts)
   int units;      // bs * parts
@@ -83,7 +84,93 @@ __device__ __forceinline__ float bound_fma(float q, float b, float acc) {
   else return __fmaf_rn(q, b, acc);
 }
 
-// The request's selection and position layout, by the whole block.
+__device__ __forceinline__ uint64_t composite_key(float score, int64_t page) {
+  return ((uint64_t)float_order_key(score) << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)page);
+}
+
+__device__ __forceinline__ uint64_t shfl64(uint64_t v, int src) {
+  const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)v, src), hi = __shfl_sync(0xffffffffu, (uint32_t)(v >> 32), src);
+  return ((uint64_t)hi << 32) | lo;
+}
+
+// A warp's running top-32 of distinct 64-bit keys, one per lane, descending
+// (lane 0 the largest; 0 = empty).  Insert x, known to beat the smallest.
+__device__ __forceinline__ void top32_insert(uint64_t& mine, uint64_t x, int lane) {
+  const int pos = __popc(__ballot_sync(0xffffffffu, mine > x));  // keys that stay ahead of x
+  const uint64_t up = shfl64(mine, lane > 0 ? lane - 1 : 0);
+  mine = lane < pos ? mine : (lane == pos ? x : up);
+}
+
+// Top 32 of the union of two descending lists, descending: the element-wise
+// max of a and reversed b is bitonic and holds the top 32; a bitonic
+// half-cleaner cascade sorts it.
+__device__ __forceinline__ uint64_t top32_merge(uint64_t a, uint64_t b, int lane) {
+  const uint64_t br = shfl64(b, 31 - lane);
+  uint64_t c = a > br ? a : br;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    const uint64_t o = shfl64(c, lane ^ d);
+    c = (lane & d) == 0 ? (c > o ? c : o) : (c < o ? c : o);
+  }
+  return c;
+}
+
+// Position layout of request i from the selected pages in score order
+// (quest.py:453-459), or the dense layout 0 .. L-1 padded with L-1
+// (quest.py:339-340); four positions per thread in flight so the
+// req_to_token reads overlap.
+__device__ void write_layout(const SelectArgs& a, int i, int64_t req, int64_t L, bool is_long, int sel,
+                             const int32_t* s_order) {
+  const qq_quest_state& st = a.st;
+  const int tid = threadIdx.x;
+  const int P = st.page_size;
+  const int top_k = st.top_k;
+  const int n = (int)(L < top_k ? L : top_k);
+  if (a.actual_lens != nullptr && tid == 0) a.actual_lens[i] = n;
+  int32_t* pos_out = a.positions + (int64_t)i * top_k;
+  int32_t* rows_out = a.rows != nullptr ? a.rows + (int64_t)i * top_k : nullptr;
+  const int32_t* r2t = a.r2t != nullptr ? a.r2t + req * a.r2t_stride : nullptr;
+  const int64_t last = L > 0 ? L - 1 : 0;
+  const int sel_req = top_k / P - 1;
+  const int64_t rp0 = L - P > 0 ? L - P : 0;
+  const int sp = sel_req * P;
+  constexpr int kU = 4;
+  for (int s0 = 0; s0 < top_k; s0 += kThreads * kU) {
+    int64_t pos[kU];
+    int32_t rv[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int s = s0 + u * kThreads + tid;
+      if (!is_long) {
+        pos[u] = s < last ? s : last;
+      } else if (s < sp) {
+        const int b = s / P;
+        const int32_t page = b < sel ? s_order[b] : (sel > 0 ? s_order[sel - 1] : 0);
+        pos[u] = (int64_t)page * P + (s - b * P);
+      } else {
+        const int64_t r = rp0 + (s - sp);
+        pos[u] = r < last ? r : last;
+      }
+    }
+    if (rows_out != nullptr) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int s = s0 + u * kThreads + tid;
+        rv[u] = (s < top_k && (is_long || s < n) && pos[u] < a.r2t_stride) ? __ldg(r2t + pos[u]) : 0;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int s = s0 + u * kThreads + tid;
+      if (s < top_k) {
+        pos_out[s] = (int32_t)pos[u];
+        if (rows_out != nullptr && (is_long || s < n)) rows_out[s] = rv[u];
+      }
+    }
+  }
+}
+
+// The request's selection (any sel, by radix select) and position layout, by the whole block.
 __device__ void select_request(const SelectArgs& a, int i, int64_t req, int64_t L, int64_t C, bool is_long,
                                unsigned char* smem, int* s_hist, int& s_digit, int& s_above, int& s_ngt) {
   const qq_quest_state& st = a.st;
@@ -91,13 +178,6 @@ __device__ void select_request(const SelectArgs& a, int i, int64_t req, int64_t 
   const int P = st.page_size;
   const int top_k = st.top_k;
   const float* scores = a.scores + (int64_t)i * st.max_pages;
-  const int n = (int)(L < top_k ? L : top_k);
-  if (a.actual_lens != nullptr && tid == 0) a.actual_lens[i] = n;
-  int32_t* pos_out = a.positions + (int64_t)i * top_k;
-  int32_t* rows_out = a.rows != nullptr ? a.rows + (int64_t)i * top_k : nullptr;
-  const int32_t* r2t = a.r2t != nullptr ? a.r2t + req * a.r2t_stride : nullptr;
-  const int64_t last = L > 0 ? L - 1 : 0;
-
   const int sel_req = top_k / P - 1;
   const int sel = is_long ? (int)min((int64_t)sel_req, C) : 0;
   uint32_t* s_okey = reinterpret_cast<uint32_t*>(smem);
@@ -184,65 +264,58 @@ __device__ void select_request(const SelectArgs& a, int i, int64_t req, int64_t 
     }
     __syncthreads();
   }
-  // layout: selected pages in score order, then the recent window
-  // (quest.py:453-459); dense 0 .. L-1 padded with L-1 (quest.py:339-340).
-  // Four positions per thread in flight so the req_to_token reads overlap.
-  const int64_t rp0 = L - P > 0 ? L - P : 0;
-  const int sp = sel_req * P;
-  constexpr int kU = 4;
-  for (int s0 = 0; s0 < top_k; s0 += kThreads * kU) {
-    int64_t pos[kU];
-    int32_t rv[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int s = s0 + u * kThreads + tid;
-      if (!is_long) {
-        pos[u] = s < last ? s : last;
-      } else if (s < sp) {
-        const int b = s / P;
-        const int32_t page = b < sel ? s_order[b] : (sel > 0 ? s_order[sel - 1] : 0);
-        pos[u] = (int64_t)page * P + (s - b * P);
-      } else {
-        const int64_t r = rp0 + (s - sp);
-        pos[u] = r < last ? r : last;
-      }
-    }
-    if (rows_out != nullptr) {
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int s = s0 + u * kThreads + tid;
-        rv[u] = (s < top_k && (is_long || s < n) && pos[u] < a.r2t_stride) ? __ldg(r2t + pos[u]) : 0;
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int s = s0 + u * kThreads + tid;
-      if (s < top_k) {
-        pos_out[s] = (int32_t)pos[u];
-        if (rows_out != nullptr && (is_long || s < n)) rows_out[s] = rv[u];
-      }
-    }
-  }
+  write_layout(a, i, req, L, is_long, sel, s_order);
 }
 
 // KW 16-byte words per lane and page, DEPTH pages in flight per warp.
 template <typename QT, int KW, int DEPTH>
 __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a) {
+  constexpr int kQPerThread = QQ_MAX_CHANNELS / kThreads;  // query-mean channels per thread
   __shared__ float s_qbar[QQ_MAX_CHANNELS];
   __shared__ int s_hist[256];
+  __shared__ uint64_t s_lists[2][kWarps][kSelectListLen];
+  __shared__ int32_t s_top[kSelectListLen];
   __shared__ int s_digit, s_above, s_last, s_ngt;
-  extern __shared__ __align__(16) unsigned char s_dyn[];  // the selection's keys and pages
+  extern __shared__ __align__(16) unsigned char s_dyn[];  // the radix selection's keys and pages
 
   const qq_quest_state& st = a.st;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nch = st.kv_heads * st.head_dim;
   const int nvec = nch >> 2;
   const size_t page_words = (size_t)nvec;  // 16-byte words per page
+  const int G = a.q_heads / st.kv_heads;
+  const int D = st.head_dim;
+  const int sel_req = st.top_k / st.page_size - 1;
+  // sel <= 32: every warp keeps the top 32 of its pages while it scores them
+  const bool lists = !a.score_all && sel_req <= kSelectListLen;
 
   for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
     const int i = u / a.parts, j = u - (u / a.parts) * a.parts;
+    // request row, length and the query rows all in flight at once
     const int64_t req = a.reqs[i];
     const int64_t L = a.score_all ? 0 : a.seq_lens[i];
+    const QT* q = static_cast<const QT*>(a.q) + (int64_t)i * a.q_stride;
+    float qsum[kQPerThread];
+#pragma unroll
+    for (int ci = 0; ci < kQPerThread; ++ci) {
+      // q̄: the GQA mean in the query dtype (quest.py:390), fp32 sum over the
+      // group in head order, eight loads in flight at a time
+      const int c = tid + ci * kThreads;
+      qsum[ci] = 0.f;
+      if (c < nch) {
+        const int h = c / D, d = c - h * D;
+        const QT* qc = q + (int64_t)h * G * D + d;
+        int g = 0;
+        for (; g + 8 <= G; g += 8) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = Elem<QT>::load(qc + (int64_t)(g + e) * D);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) qsum[ci] = __fadd_rn(qsum[ci], v[e]);
+        }
+        for (; g < G; ++g) qsum[ci] = __fadd_rn(qsum[ci], Elem<QT>::load(qc + (int64_t)g * D));
+      }
+    }
     int64_t F, C;
     bool is_long;
     if (a.score_all) {
@@ -260,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     const uint4* bounds = reinterpret_cast<const uint4*>(st.page_bounds) +
                           ((size_t)a.layer * st.max_reqs + req) * st.max_pages * page_words;
 
-    // the first DEPTH pages of this warp in flight before anything else
+    // the first DEPTH pages of this warp in flight
     uint4 buf[DEPTH][KW];
     auto load_page = [&](uint4 (&w)[KW], int64_t p) {
       const uint4* src = bounds + (size_t)p * page_words;
@@ -286,26 +359,12 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     }
 
     // (b) scores of the part's candidate pages
+    uint64_t top = 0, top_min = 0;  // this warp's top 32 (lists), and its smallest
     if (pg0 < p_end) {
-      // q̄: the GQA mean in the query dtype (quest.py:390), fp32 sum over the
-      // group in head order, eight loads in flight at a time
-      const QT* q = static_cast<const QT*>(a.q) + (int64_t)i * a.q_stride;
-      const int G = a.q_heads / st.kv_heads;
-      const int D = st.head_dim;
-      for (int c = tid; c < nch; c += kThreads) {
-        const int h = c / D, d = c - h * D;
-        const QT* qc = q + (int64_t)h * G * D + d;
-        float acc = 0.f;
-        int g = 0;
-        for (; g + 8 <= G; g += 8) {
-          float v[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = Elem<QT>::load(qc + (int64_t)(g + e) * D);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, v[e]);
-        }
-        for (; g < G; ++g) acc = __fadd_rn(acc, Elem<QT>::load(qc + (int64_t)g * D));
-        s_qbar[c] = G == 1 ? acc : Elem<QT>::round(__fdiv_rn(acc, (float)G));
+      for (int ci = 0; ci < kQPerThread; ++ci) {
+        const int c = tid + ci * kThreads;
+        if (c < nch) s_qbar[c] = G == 1 ? qsum[ci] : Elem<QT>::round(__fdiv_rn(qsum[ci], (float)G));
       }
       __syncthreads();
       float qv[KW][4];
@@ -336,10 +395,18 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
             // the next page of this slot goes in flight before the reduction
             const int64_t pn = p + DEPTH * kWarps;
             if (pn < p_end) load_page(buf[d], pn);
+            // butterfly sum: every lane ends with the same value
             float sum = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
             if (lane == 0) scores[p] = sum;
+            if (lists) {
+              const uint64_t key = composite_key(sum, p);
+              if (key > top_min) {
+                top32_insert(top, key, lane);
+                top_min = shfl64(top, 31);
+              }
+            }
           }
         }
       }
@@ -351,10 +418,51 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
       for (int64_t p = m0 + tid; p < m1; p += kThreads) scores[p] = -__int_as_float(0x7f800000);
     }
 
-    // (c) the block arrives on the request's counter; the last part to
-    // arrive does the selection.  The barrier and thread 0's fence order
-    // every thread's score writes before the arrival, and the last arriver's
-    // fence orders its reads after it.
+    const int sel = is_long ? (int)min((int64_t)sel_req, C) : 0;
+    if (lists) {
+      // the part's top 32: a merge tree over the warps' lists
+      s_lists[0][warp][lane] = top;
+      __syncthreads();
+      int cur = 0;
+      for (int n = kWarps; n > 1; n >>= 1) {
+        if (warp < n / 2)
+          s_lists[cur ^ 1][warp][lane] = top32_merge(s_lists[cur][2 * warp][lane], s_lists[cur][2 * warp + 1][lane], lane);
+        cur ^= 1;
+        __syncthreads();
+      }
+      top = s_lists[cur][0][lane];
+      if (a.parts > 1) {
+        // publish the part's list; the barrier and thread 0's fence order
+        // every thread's writes before the arrival, the last arriver's fence
+        // orders its reads after it
+        if (warp == 0) a.lists[(size_t)u * kSelectListLen + lane] = top;
+        __syncthreads();
+        if (tid == 0) {
+          __threadfence();
+          const bool last = atomicAdd(&a.counters[i], 1) == a.parts - 1;
+          if (last) {
+            __threadfence();
+            a.counters[i] = 0;
+          }
+          s_last = last;
+        }
+        __syncthreads();
+        if (!s_last) continue;
+        if (warp == 0) {
+          top = 0;
+          for (int jj = 0; jj < a.parts; ++jj)
+            top = top32_merge(top, __ldcg(a.lists + ((size_t)i * a.parts + jj) * kSelectListLen + lane), lane);
+        }
+      }
+      if (warp == 0 && lane < sel) s_top[lane] = (int32_t)(0xFFFFFFFFu - (uint32_t)(top & 0xFFFFFFFFu));
+      __syncthreads();
+      write_layout(a, i, req, L, is_long, sel, s_top);
+      __syncthreads();  // s_lists and s_top are free again
+      continue;
+    }
+
+    // (c) sel > 32: the block arrives on the request's counter; the last
+    // part to arrive does the radix selection.
     __syncthreads();
     if (tid == 0) {
       __threadfence();
@@ -490,6 +598,7 @@ extern "C" int qq_quest_retrieve_topk(const qq_quest_state* st, int layer, const
   a.r2t_stride = translate ? translate->stride : 0;
   a.rows = rows;
   a.counters = ws_counters(workspace, kCounterSelect);
+  a.lists = ws_select_lists(workspace);
   if (nt != nullptr && nt->k != nullptr) {
     const int esz = nt->dtype == QQ_F32 ? 4 : 2;
     const int64_t row_bytes = (int64_t)st->kv_heads * st->head_dim * esz;
