@@ -81,7 +81,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
             return
@@ -308,7 +308,7 @@ def measured_peaks() -> tuple[float, str]:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--seed", type=int, default=0)
@@ -355,32 +355,44 @@ def main() -> None:
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     total = args.warmup + args.steps
-    # two passes of the timed steps: value (inputs resident) and e2e (host inputs)
+    # three passes of the timed steps: value (inputs resident), per-kernel
+    # events (inputs resident) and e2e (host inputs)
     n_req, n_layers = args.requests, args.layers
-    backend, pool, r2t, max_ctx, qkv = build_config1(dev, 2 * total + 1, args.seed + 1000 * rank, n_req=n_req,
+    backend, pool, r2t, max_ctx, qkv = build_config1(dev, 3 * total + 1, args.seed + 1000 * rank, n_req=n_req,
                                                      layers=n_layers, resident=min(args.resident, n_layers))
-    batches, layers = make_batches(dev, backend, pool, r2t, max_ctx, 2 * total + 1, n_req=n_req)
+    batches, layers = make_batches(dev, backend, pool, r2t, max_ctx, 3 * total + 1, n_req=n_req)
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
 
-    # ---- value: device-resident inputs
+    # ---- value: device-resident inputs, nothing but the step in the timed region
     for s in range(args.warmup):
         run_step(backend, batches[s], layers, qkv)
     barrier()
-    backend.kernel_events = {}
     clocks = ClockSampler(dev.index if world == 1 else local_rank)
     clocks.start()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
+    torch.cuda.nvtx.range_push("timed_value")  # profilers select the timed steps by this range
     for s in range(args.warmup, total):
         run_step(backend, batches[s], layers, qkv)
+    torch.cuda.nvtx.range_pop()
     end.record()
     barrier()
     clock_info = clocks.stop()
     ms = start.elapsed_time(end)
+    backend.check_errors()
+
+    # ---- per-kernel durations (CUDA events on the launching stream), same steps again
+    for s in range(total, total + args.warmup):
+        run_step(backend, batches[s], layers, qkv)
+    barrier()
+    backend.kernel_events = {}
+    for s in range(total + args.warmup, 2 * total):
+        run_step(backend, batches[s], layers, qkv)
+    barrier()
     kev = backend.kernel_events
     backend.kernel_events = None
     kernel_ms = {k: statistics.mean(a.elapsed_time(b) for a, b in v) for k, v in kev.items()}
@@ -393,11 +405,11 @@ def main() -> None:
     hout = torch.empty((n_layers, n_req, H * D), dtype=torch.bfloat16).pin_memory()
     dq, dk, dv = torch.empty_like(qs), torch.empty_like(ks), torch.empty_like(vs)
     e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for s in range(total, total + args.warmup):
+    for s in range(2 * total, 2 * total + args.warmup):
         run_step(backend, batches[s], layers, qkv)
     barrier()
     e2e_start.record()
-    for s in range(total + args.warmup, 2 * total):
+    for s in range(2 * total + args.warmup, 3 * total):
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
