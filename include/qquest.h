@@ -123,7 +123,9 @@ typedef struct qq_hisparse_state {
 int qq_host_device_pointer(const void* host_ptr, void** device_ptr);
 const char* qq_version(void);
 const char* qq_status_string(int status);
-/* Workspace bytes for calls with up to max_bs requests. */
+/* Workspace bytes for calls with up to max_bs requests (any of the calls
+ * below that take a workspace; one workspace may serve all of them when
+ * the calls are ordered on one stream). */
 size_t qq_workspace_bytes(int max_bs, int top_k, int q_heads, int head_dim);
 
 /* ---- storage initialisation ------------------------------------------ */
@@ -201,8 +203,9 @@ int qq_quest_retrieve_topk(const qq_quest_state* st, int layer, const qq_batch* 
 /* ---- [Q7] sparse decode attention ------------------------------------ */
 /* out[b] = attention of q[b] ([q_heads][head_dim]) over the rows
  * rows[b][0 .. min(seq_len, top_k)) of k_pool / v_pool (duplicates counted),
- * fp32 softmax and accumulation, result in the query dtype.  Split over
- * 128-row chunks, merged in-kernel.  Replaces decode_attention
+ * fp32 softmax and accumulation, result in the query dtype.  The rows of
+ * all requests are split into equal per-warp shares; segments cut by a
+ * share boundary are merged in-kernel.  Replaces decode_attention
  * (attention/ops.py:48-66) as called by QuestOnlyBackend.forward_decode
  * (quest_only.py:153-158) and QuestHiSparseBackend.forward_decode
  * (quest_hisparse.py:128-132). */

@@ -60,6 +60,13 @@ class Scenario:
     seed: int = 0
     #: number of pages whose keys are pulled towards the request's query mean
     planted_pages: int = 2
+    #: > 0: K = scale * (W + N(0,1)) with W a per-(layer, head, channel)
+    #: random walk along the positions, steps N(0, k_walk^2) (benchmark config 2)
+    k_walk: float = 0.0
+    #: > 0: decode queries follow q[t+1] = q_ar * q[t] + N(0,1) (benchmark config 3)
+    q_ar: float = 0.0
+    #: generate q only for decode positions (>= prompt length); prefill must be "direct"
+    q_decode_only: bool = False
     extra: dict = field(default_factory=dict, hash=False, compare=False)
 
     @property
@@ -78,14 +85,34 @@ class Scenario:
         return d
 
 
+class OffsetRows:
+    """``[layers, positions, ...]`` rows that start at position ``start``: ``x[layer, p]`` is position ``p``."""
+
+    def __init__(self, rows: np.ndarray, start: int):
+        self.rows, self.start = rows, start
+
+    def __getitem__(self, key):
+        layer, pos = key
+        if isinstance(pos, slice):
+            if self.start and (pos.start or 0) < self.start:
+                raise IndexError("rows before the first generated position")
+            return self.rows[layer, slice((pos.start or 0) - self.start,
+                                          None if pos.stop is None else pos.stop - self.start)]
+        return self.rows[layer, pos - self.start]
+
+
 def scenario_tensors(sc: Scenario, req: int) -> dict[str, np.ndarray]:
     """Seeded ``q/k/v`` of request ``req`` (admission-order index) for every position.
 
     Returns float32 arrays ``k, v: [layers, total, kv_heads, head_dim]`` and
     ``q: [layers, total, q_heads, head_dim]`` with ``total = prompt + new
     tokens``; bf16-exact when ``sc.bf16``.  Row ``t`` is the token at
-    position ``t``; ``q`` rows of prompt positions feed prefill.
+    position ``t``; ``q`` rows of prompt positions feed prefill.  With
+    ``sc.q_decode_only`` ``q`` is an :class:`OffsetRows` of the decode
+    positions only.
     """
+    if sc.k_walk or sc.q_ar or sc.q_decode_only:
+        return _scenario_tensors_v2(sc, req)
     total = sc.prompt_lens[req] + sc.new_tokens[req]
     rng = np.random.default_rng([sc.seed, req])
     L, H, KV, D = sc.layers, sc.q_heads, sc.kv_heads, sc.head_dim
@@ -108,6 +135,43 @@ def scenario_tensors(sc: Scenario, req: int) -> dict[str, np.ndarray]:
     if sc.bf16:
         q, k, v = _round_bf16_np(q), _round_bf16_np(k), _round_bf16_np(v)
     return {"q": q, "k": k, "v": v}
+
+
+def _scenario_tensors_v2(sc: Scenario, req: int) -> dict:
+    """The benchmark's config-2 / config-3 distributions (see :class:`Scenario`)."""
+    prompt = sc.prompt_lens[req]
+    total = prompt + sc.new_tokens[req]
+    rng = np.random.default_rng([sc.seed, req, 2])
+    L, H, KV, D = sc.layers, sc.q_heads, sc.kv_heads, sc.head_dim
+    scale = rng.lognormal(0.0, 0.5, size=(L, 1, KV, D)).astype(np.float32)
+    k = rng.standard_normal((L, total, KV, D), dtype=np.float32)
+    if sc.k_walk:
+        walk = rng.standard_normal((L, total, KV, D), dtype=np.float32)
+        walk *= np.float32(sc.k_walk)
+        np.cumsum(walk, axis=1, out=walk)
+        k += walk
+        del walk
+    k *= scale
+    v = rng.standard_normal((L, total, KV, D), dtype=np.float32) * scale
+    q0 = prompt if sc.q_decode_only else 0
+    q = rng.standard_normal((L, total - q0, H, D), dtype=np.float32)
+    if sc.q_ar:
+        first = prompt - q0  # the first decode query keeps its N(0,1) draw
+        for t in range(first + 1, total - q0):
+            q[:, t] += np.float32(sc.q_ar) * q[:, t - 1]
+    if sc.planted_pages and prompt >= 2 * sc.page_size:
+        group = H // KV
+        qd = q[:, prompt - q0]
+        if sc.bf16:
+            qd = _round_bf16_np(qd)
+        qbar = qd.reshape(L, KV, group, D).mean(axis=2)
+        full = prompt // sc.page_size
+        pages = rng.choice(full, size=min(sc.planted_pages, full), replace=False)
+        for p in pages.tolist():
+            k[:, p * sc.page_size:(p + 1) * sc.page_size] += 0.5 * qbar[:, None]
+    if sc.bf16:
+        q, k, v = _round_bf16_np(q), _round_bf16_np(k), _round_bf16_np(v)
+    return {"q": OffsetRows(q, q0) if q0 else q, "k": k, "v": v}
 
 
 # --------------------------------------------------------------------------- #

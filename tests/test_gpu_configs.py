@@ -1,0 +1,58 @@
+"""Benchmark configs 2 and 3 at their context lengths, against the oracle (GPU).
+
+* Config 2 (Mode 2): ragged long contexts in [65536, 131072] that end in a
+  partial page, keys with a slow random-walk drift (step sigma 0.02) plus
+  N(0,1) noise, and two dense-fallback requests, one of which crosses
+  top_k = 2048 into the sparse path.  A six-request sample of the config's
+  sixteen keeps the oracle's bounds and attention within seconds.
+* Config 3 (Mode 3, HiSparse): 65536-token requests with the full KV in the
+  pinned host tier, a 4096 + 1 slot hot buffer, and decode queries that
+  follow an AR(1) process (rho 0.9), so each step misses part of its
+  selection; three requests over 24 decode steps.
+
+Selections must equal the oracle's (near-ties excused and counted), the hot
+buffer state bit-exact, attention within 2e-2 (bf16).
+"""
+
+from __future__ import annotations
+
+import pytest
+
+from qwenquest_b200.harness import LifecycleDriver, b200_api, records_to_arrays
+from qwenquest_b200.workloads import Scenario
+from tests.parity_helpers import compare_runs, oracle_run
+
+pytestmark = pytest.mark.gpu
+
+CONFIG2_SAMPLE = Scenario(
+    name="config2_sample", layers=1, q_heads=32, kv_heads=4, head_dim=128, bf16=True,
+    top_k=2048, page_size=64, device_buffer_size=4096,
+    prompt_lens=(70001, 98765, 131000, 65601, 1500, 2046), new_tokens=(4, 4, 4, 4, 4, 4),
+    max_running=6, max_context_len=131072, seed=2, planted_pages=0, k_walk=0.02, q_decode_only=True,
+)
+CONFIG3_SAMPLE = Scenario(
+    name="config3_sample", layers=1, q_heads=32, kv_heads=4, head_dim=128, bf16=True,
+    top_k=2048, page_size=64, device_buffer_size=4096,
+    prompt_lens=(65536, 65536, 65536), new_tokens=(25, 25, 25),
+    max_running=3, max_context_len=65536 + 64, seed=3, planted_pages=0, q_ar=0.9, q_decode_only=True,
+)
+
+
+@pytest.mark.parametrize(("sc", "mode"), [(CONFIG2_SAMPLE, "quest"), (CONFIG3_SAMPLE, "quest_hisparse")],
+                         ids=["config2", "config3"])
+def test_benchmark_config_matches_oracle(sc, mode, cuda_device):
+    drv = LifecycleDriver(sc, mode, b200_api(), cuda_device, prefill="direct")
+    recs = drv.run()
+    drv.backend.synchronize()
+    ours = records_to_arrays(recs, sc.top_k)
+    orecs, ref, ostats = oracle_run(sc, mode)
+    rep = compare_runs(ours, ref, orecs, top_k=sc.top_k, page_size=sc.page_size, bf16=sc.bf16,
+                       check_buffers=True)
+    print(f"{sc.name}/{mode}: {rep.summary()} stats={drv.stats()} oracle={ostats}")
+    assert rep.ok(), rep.summary() + "\n" + "\n".join(rep.failures)
+    assert rep.exact >= 0.9 * rep.records, rep.summary()
+    if mode == "quest_hisparse":
+        stats = drv.stats()
+        assert stats["misses"] > 0 and stats["hits"] > 0
+        if rep.excused == 0:
+            assert stats == ostats
