@@ -256,6 +256,8 @@ struct StreamCfg {
 template <int WARPS, int SLOTS>
 __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) {
   using Cfg = StreamCfg<WARPS, SLOTS>;
+  wait_prior_grid();
+  allow_next_grid();
   extern __shared__ __align__(128) char smem[];
   int32_t* s_prefix4 = reinterpret_cast<int32_t*>(smem + Cfg::kRing);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -614,8 +616,7 @@ int launch_stream_variant(const AttnArgs& a, cudaStream_t s) {
       return QQ_ERR_CUDA;
     attr_set = true;
   }
-  attn_stream_kernel<WARPS, SLOTS><<<sm_count(), Cfg::kThreads, Cfg::kSmem, s>>>(a);
-  return launch_status();
+  return launch_pdl(attn_stream_kernel<WARPS, SLOTS>, dim3(sm_count()), dim3(Cfg::kThreads), Cfg::kSmem, s, a);
 }
 
 // Warps per block x ring slots per warp.  QQ_ATTN_VARIANT (e.g. "12x2") picks

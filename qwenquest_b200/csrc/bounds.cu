@@ -135,6 +135,8 @@ struct StepArgs {
 // block can observe the advanced values (quest.py:304-321).
 template <typename T>
 __global__ void decode_step_kernel(StepArgs a) {
+  wait_prior_grid();
+  allow_next_grid();
   const int i = blockIdx.x;
   const int g = blockIdx.y;
   const qq_quest_state& st = a.st;
@@ -309,9 +311,6 @@ extern "C" int qq_quest_decode_step(const qq_quest_state* st, int flags, int lay
   a.counters = ws_counters(workspace, kCounterStep);
   dim3 grid(batch->bs, a.groups);
   cudaStream_t s = as_stream(stream);
-  if (kv_dtype == QQ_F32)
-    decode_step_kernel<float><<<grid, 128, 0, s>>>(a);
-  else
-    decode_step_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(a);
-  return launch_status();
+  if (kv_dtype == QQ_F32) return launch_pdl(decode_step_kernel<float>, grid, dim3(128), 0, s, a);
+  return launch_pdl(decode_step_kernel<__nv_bfloat16>, grid, dim3(128), 0, s, a);
 }

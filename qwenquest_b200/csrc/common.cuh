@@ -1,6 +1,8 @@
 // Shared device helpers for the Quest kernels (sm_100a).
 #pragma once
 
+#include <cstdlib>
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -158,9 +160,49 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
   return r;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+//
+// The decode-step kernels are launched with programmatic stream
+// serialization: a kernel's blocks may be dispatched while the previous
+// kernel in the stream finishes, and each block waits in wait_prior_grid()
+// (griddepcontrol.wait: the previous grid has completed and its writes are
+// visible) before it reads anything.  Without the launch attribute the wait
+// returns at once.
+
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel in the stream be dispatched once every block of this
+// one has started (or exited); its blocks still wait for this grid to finish.
+__device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- host helpers
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// QQ_PDL=0 in the environment launches without the attribute (for comparisons).
+inline bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("QQ_PDL");
+    on = (v != nullptr && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) == cudaSuccess ? QQ_OK : QQ_ERR_CUDA;
+}
 
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();

@@ -278,6 +278,8 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
   __shared__ int s_digit, s_above, s_last, s_ngt;
   extern __shared__ __align__(16) unsigned char s_dyn[];  // the radix selection's keys and pages
 
+  wait_prior_grid();
+  allow_next_grid();
   const qq_quest_state& st = a.st;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nch = st.kv_heads * st.head_dim;
@@ -521,12 +523,11 @@ int launch_select(const SelectArgs& a, int grid, int kw, size_t smem, cudaStream
     attr_smem = smem;
   }
   switch (kw) {
-    case 1: score_select_kernel<QT, 1, 4><<<grid, kThreads, smem, s>>>(a); break;
-    case 2: score_select_kernel<QT, 2, 4><<<grid, kThreads, smem, s>>>(a); break;
-    case 4: score_select_kernel<QT, 4, 3><<<grid, kThreads, smem, s>>>(a); break;
-    default: score_select_kernel<QT, 8, 1><<<grid, kThreads, smem, s>>>(a); break;
+    case 1: return launch_pdl(score_select_kernel<QT, 1, 4>, dim3(grid), dim3(kThreads), smem, s, a);
+    case 2: return launch_pdl(score_select_kernel<QT, 2, 4>, dim3(grid), dim3(kThreads), smem, s, a);
+    case 4: return launch_pdl(score_select_kernel<QT, 4, 3>, dim3(grid), dim3(kThreads), smem, s, a);
+    default: return launch_pdl(score_select_kernel<QT, 8, 1>, dim3(grid), dim3(kThreads), smem, s, a);
   }
-  return launch_status();
 }
 
 bool valid_state(const qq_quest_state* st) {
