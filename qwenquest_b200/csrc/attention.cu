@@ -226,10 +226,10 @@ __device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, co
 #pragma unroll
     for (int k = 0; k < kToks; ++k) r[k] = k < w.cnt ? r[k] : 0u;
   }
-  bool bad = false;
-#pragma unroll
-  for (int k = 0; k < kToks; ++k) bad |= r[k] > max_row;
-  if (bad) {
+  // lane l (< cnt) checks row l; the broadcast copies above give every lane all 16
+  const int own = threadIdx.x & 15;
+  const uint32_t own_row = own < w.cnt ? (uint32_t)__ldg(a.rows + (int64_t)w.s_req * a.top_k + w.r0 + own) : 0u;
+  if (__any_sync(0xffffffffu, own_row > max_row)) {
     raise_error(a.err, QQ_DEV_ERR_BOUNDS);
 #pragma unroll
     for (int k = 0; k < kToks; ++k) r[k] = r[k] > max_row ? 0u : r[k];
@@ -355,14 +355,19 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
     const char* sv = sk + kToks * kPitch;
     slot = slot + 1 == SLOTS ? 0 : slot + 1;
     // ---- S^T = K . Q^T
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    // two accumulators (even / odd k-steps) halve the dependent MMA chain
+    float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t kaddr = smem_u32(sk + (lane & 15) * kPitch + (lane >> 4) * 16);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      uint32_t a0, a1, a2, a3;
+    for (int kk = 0; kk < 8; kk += 2) {
+      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
       ldmatrix_x4(a0, a1, a2, a3, kaddr + kk * 32);
+      ldmatrix_x4(b0, b1, b2, b3, kaddr + (kk + 1) * 32);
       mma_bf16_16816(c, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      mma_bf16_16816(c2, b0, b1, b2, b3, qb[kk + 1][0], qb[kk + 1][1]);
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[e] += c2[e];
     // ---- online softmax (exp2 domain); rows >= ntok are masked
     const bool v0 = gid < ntok, v1 = gid + 8 < ntok;
     const float s00 = v0 ? c[0] * a.scale_log2 : kNegInf;  // row gid, head 2tig
@@ -477,19 +482,32 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
     __threadfence();
     if (lane == 0) a.seg_count[seg_id] = 0;
     const int hq = lane >> 2;
-    // warp w_first holds the segment in record 1 unless its share starts at the segment
+    // record r of the segment: warp w_first + r; warp w_first holds it in
+    // record 1 unless its share starts at the segment.  The records' loads
+    // are issued in batches so that their L2 latencies overlap.
     const int first_slot = sp.begin(w_first) != seg0 ? 1 : 0;
-    float M = kNegInf;
-    for (int w = w_first; w <= w_last; ++w) {
-      const int sl = w == w_first ? first_slot : 0;
-      M = fmaxf(M, __ldcg(a.part + ((int64_t)w * 2 + sl) * kPartFloats + kG * kD + hq * 2));
-    }
-    float S = 0.f;
-    for (int w = w_first; w <= w_last; ++w) {
-      const int sl = w == w_first ? first_slot : 0;
-      const float* ml = a.part + ((int64_t)w * 2 + sl) * kPartFloats + kG * kD + hq * 2;
-      const float mw = __ldcg(ml);
-      S += mw == kNegInf ? 0.f : __ldcg(ml + 1) * fast_exp2(mw - M);
+    const int nrec = w_last - w_first + 1;
+    auto rec_of = [&](int r) -> const float* {
+      return a.part + ((int64_t)(w_first + r) * 2 + (r == 0 ? first_slot : 0)) * kPartFloats;
+    };
+    // (m, l) of this lane's head, eight records at a time: running max M and sum S
+    constexpr int kMB = 8;
+    float M = kNegInf, S = 0.f;
+    for (int r0 = 0; r0 < nrec; r0 += kMB) {
+      float2 ml[kMB];
+#pragma unroll
+      for (int j = 0; j < kMB; ++j)
+        ml[j] = r0 + j < nrec ? __ldcg(reinterpret_cast<const float2*>(rec_of(r0 + j) + kG * kD + hq * 2))
+                              : make_float2(kNegInf, 0.f);
+      float Mb = M;
+#pragma unroll
+      for (int j = 0; j < kMB; ++j) Mb = fmaxf(Mb, ml[j].x);
+      if (Mb != kNegInf) {
+        S *= fast_exp2(M - Mb);
+#pragma unroll
+        for (int j = 0; j < kMB; ++j) S += ml[j].x == kNegInf ? 0.f : ml[j].y * fast_exp2(ml[j].x - Mb);
+      }
+      M = Mb;
     }
     const float inv = 1.f / S;
 #pragma unroll
@@ -498,19 +516,34 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       float o[16];
 #pragma unroll
       for (int e = 0; e < 16; ++e) o[e] = 0.f;
-      for (int w = w_first; w <= w_last; ++w) {
-        const int sl = w == w_first ? first_slot : 0;
-        const float* rw = a.part + ((int64_t)w * 2 + sl) * kPartFloats;
-        const float mw = __ldcg(rw + kG * kD + hq * 2);
-        const float f = mw == kNegInf ? 0.f : fast_exp2(mw - M);
-        const float4* src = reinterpret_cast<const float4*>(rw + hq * kD + c0);
+      constexpr int kOB = 4;  // records whose 16 channels are in flight together
+      for (int r0 = 0; r0 < nrec; r0 += kOB) {
+        float mr[kOB];
+        float4 x[kOB][4];
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const float4 x = __ldcg(src + v);
-          o[4 * v] += f * x.x;
-          o[4 * v + 1] += f * x.y;
-          o[4 * v + 2] += f * x.z;
-          o[4 * v + 3] += f * x.w;
+        for (int j = 0; j < kOB; ++j) {
+          if (r0 + j < nrec) {
+            const float* rw = rec_of(r0 + j);
+            mr[j] = __ldcg(rw + kG * kD + hq * 2);
+            const float4* src = reinterpret_cast<const float4*>(rw + hq * kD + c0);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) x[j][v] = __ldcg(src + v);
+          } else {
+            mr[j] = kNegInf;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) x[j][v] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kOB; ++j) {
+          const float f = mr[j] == kNegInf ? 0.f : fast_exp2(mr[j] - M);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            o[4 * v] += f * x[j][v].x;
+            o[4 * v + 1] += f * x[j][v].y;
+            o[4 * v + 2] += f * x[j][v].z;
+            o[4 * v + 3] += f * x[j][v].w;
+          }
         }
       }
       __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)cc.s_req * a.out_stride +
