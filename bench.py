@@ -228,12 +228,16 @@ def run_step(backend, batch, layers, qkv):
 # --------------------------------------------------------------------------- CPU baseline
 
 
-def cpu_baseline(sample_reqs: int = 2, min_seconds: float = 10.0, seed: int = 0) -> dict:
-    """The numpy oracle on a bounded sample of config 1: ``sample_reqs`` requests, one layer."""
+def _cpu_sample(sample_reqs: int, min_seconds: float, seed: int, samples: int = 1) -> list[tuple[int, float]]:
+    """One worker: the numpy oracle on ``sample_reqs`` requests x one layer of config 1;
+    ``samples`` consecutive timings of >= ``min_seconds`` each, as (repetitions, seconds)."""
+    from threadpoolctl import threadpool_limits
+
     from oracle.attention import decode_attention
     from oracle.bf16 import round_bf16
     from oracle.quest import OracleQuest
 
+    threadpool_limits(1)  # one core per worker process
     rng = np.random.default_rng(seed)
     n = PREFIX + 1
     scale = rng.lognormal(0, 0.5, size=(1, KV, D)).astype(np.float32)
@@ -246,33 +250,57 @@ def cpu_baseline(sample_reqs: int = 2, min_seconds: float = 10.0, seed: int = 0)
         oq.update_prefill_representations(0, i, ks[i], np.arange(PREFIX))
     reqs = np.arange(sample_reqs)
     seq = np.full(sample_reqs, n)
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        # the per-step bounds fold of the previous token; counters reset so repetitions stay in range
-        oq.running_token_count[:] = 0
-        oq.running_page_idx[:] = PREFIX // PAGE
-        oq.update_decode_representations(0, reqs, np.stack([k[n - 2] for k in ks]), np.arange(sample_reqs))
-        oq.maybe_finalize_decode_representations(reqs)
-        oq.prepare_step(seq)
-        pos, actual = oq.retrieve_topk(q, 0, reqs, query_is_bf16=True)
-        for i in range(sample_reqs):
-            r = pos[i, : actual[i]].astype(np.int64)
-            decode_attention(q[i], ks[i][r], vs[i][r], D ** -0.5, out_bf16=True)
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= min_seconds:
-            break
-    per_req_layer = el / (reps * sample_reqs)
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return {
-        "value": 1.0 / (per_req_layer * N_REQ),
-        "unit": UNIT,
-        "cores": threads,
-        "kind": "port",
-        "sample": f"{reps} repetitions x {sample_reqs} requests x 1 layer of config 1 (numpy oracle, "
-                  f"BLAS threads up to {threads}), scaled to the 64-request layer-step",
-        "ms_per_request_layer": per_req_layer * 1e3,
-    }
+    out = []
+    for _ in range(samples):
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            # the per-step bounds fold of the previous token; counters reset so repetitions stay in range
+            oq.running_token_count[:] = 0
+            oq.running_page_idx[:] = PREFIX // PAGE
+            oq.update_decode_representations(0, reqs, np.stack([k[n - 2] for k in ks]), np.arange(sample_reqs))
+            oq.maybe_finalize_decode_representations(reqs)
+            oq.prepare_step(seq)
+            pos, actual = oq.retrieve_topk(q, 0, reqs, query_is_bf16=True)
+            for i in range(sample_reqs):
+                r = pos[i, : actual[i]].astype(np.int64)
+                decode_attention(q[i], ks[i][r], vs[i][r], D ** -0.5, out_bf16=True)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= min_seconds:
+                break
+        out.append((reps, el))
+    return out
+
+
+def host_cores() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def cpu_baseline(min_seconds: float = 10.0, seed: int = 0, samples: int = 1, sample_reqs: int = 1) -> list[dict]:
+    """The numpy oracle (the reference's algorithm) on all host cores: one single-threaded
+    worker process per core (spawned), each timing ``samples`` consecutive bounded samples of
+    config 1 (``sample_reqs`` requests x one layer, >= ``min_seconds`` each); a sample's
+    throughput is the sum over the workers, scaled to the 64-request layer-step."""
+    import multiprocessing as mproc
+
+    workers = host_cores()
+    with mproc.get_context("spawn").Pool(workers) as pool:
+        res = pool.starmap(_cpu_sample, [(sample_reqs, min_seconds, seed + w, samples) for w in range(workers)])
+    lines = []
+    for k in range(samples):
+        req_layers_per_s = sum(r[k][0] * sample_reqs / r[k][1] for r in res)
+        reps = sum(r[k][0] for r in res)
+        lines.append({
+            "value": req_layers_per_s / N_REQ,
+            "unit": UNIT,
+            "cores": workers,
+            "kind": "port",
+            "sample": f"{workers} single-threaded worker processes x {sample_reqs} request x 1 layer of "
+                      f"config 1, {reps} repetitions in >= {min_seconds:.1f} s (numpy oracle), scaled to "
+                      f"the 64-request layer-step",
+            "ms_per_request_layer": 1e3 * workers / req_layers_per_s,
+        })
+    return lines
 
 
 def cpu_model() -> str:
@@ -332,9 +360,8 @@ def main() -> None:
             return
         torch.set_num_threads(os.cpu_count() or 1)
         t0 = time.perf_counter()
-        steps = []
-        for _ in range(args.warmup + args.steps):
-            steps.append(cpu_baseline(min_seconds=max(1.0, args.cpu_seconds / max(1, args.steps))))
+        steps = cpu_baseline(min_seconds=max(1.0, args.cpu_seconds / max(1, args.steps)),
+                             samples=args.warmup + args.steps)
         timed = steps[args.warmup:]
         value = statistics.mean(s["value"] for s in timed)
         cb = dict(timed[0])
@@ -484,7 +511,7 @@ def main() -> None:
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
-        line["cpu_baseline"] = cpu_baseline(min_seconds=args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(min_seconds=args.cpu_seconds)[0]
         line["config"]["cpu"] = cpu_model()
     if rank == 0:
         print(json.dumps(line))
