@@ -209,40 +209,54 @@ __device__ __forceinline__ bool walk_next(const Split& sp, Walk& w) {
 // QQ_DEV_ERR_BOUNDS and is replaced by row 0.  Rows past the end of a short
 // stage are zero-filled by the copy (0 * V stays 0).
 // (256-byte bulk copies on an mbarrier measured slower for this gather.)
-__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, const char* lane_pool,
-                                            uint32_t lane_dst, uint32_t stride, uint32_t max_row) {
+struct StageRows {
+  uint32_t r[kToks];  // the stage's 16 row indices (every lane)
+  uint32_t own;       // row threadIdx % 16 of the stage, 0 past cnt
+};
+
+__device__ __forceinline__ void load_stage_rows(const AttnArgs& a, const Walk& w, StageRows& s) {
   const int4* rp = reinterpret_cast<const int4*>(a.rows + (int64_t)w.s_req * a.top_k + w.r0);
-  uint32_t r[kToks];
 #pragma unroll
   for (int i = 0; i < kToks / 4; ++i) {
     const int4 x = __ldg(rp + i);
-    r[4 * i] = (uint32_t)x.x;
-    r[4 * i + 1] = (uint32_t)x.y;
-    r[4 * i + 2] = (uint32_t)x.z;
-    r[4 * i + 3] = (uint32_t)x.w;
+    s.r[4 * i] = (uint32_t)x.x;
+    s.r[4 * i + 1] = (uint32_t)x.y;
+    s.r[4 * i + 2] = (uint32_t)x.z;
+    s.r[4 * i + 3] = (uint32_t)x.w;
   }
+  const int own = threadIdx.x & 15;
+  s.own = own < w.cnt ? (uint32_t)__ldg(a.rows + (int64_t)w.s_req * a.top_k + w.r0 + own) : 0u;
+}
+
+__device__ __forceinline__ void copy_stage(const AttnArgs& a, const Walk& w, StageRows& s, const char* lane_pool,
+                                           uint32_t lane_dst, uint32_t stride, uint32_t max_row) {
   const bool full = w.cnt == kToks;
   if (!full) {
 #pragma unroll
-    for (int k = 0; k < kToks; ++k) r[k] = k < w.cnt ? r[k] : 0u;
+    for (int k = 0; k < kToks; ++k) s.r[k] = k < w.cnt ? s.r[k] : 0u;
   }
-  // lane l (< cnt) checks row l; the broadcast copies above give every lane all 16
-  const int own = threadIdx.x & 15;
-  const uint32_t own_row = own < w.cnt ? (uint32_t)__ldg(a.rows + (int64_t)w.s_req * a.top_k + w.r0 + own) : 0u;
-  if (__any_sync(0xffffffffu, own_row > max_row)) {
+  // lane l (< cnt) checks row l; the broadcast loads give every lane all 16
+  if (__any_sync(0xffffffffu, s.own > max_row)) {
     raise_error(a.err, QQ_DEV_ERR_BOUNDS);
 #pragma unroll
-    for (int k = 0; k < kToks; ++k) r[k] = r[k] > max_row ? 0u : r[k];
+    for (int k = 0; k < kToks; ++k) s.r[k] = s.r[k] > max_row ? 0u : s.r[k];
   }
   const char* src = lane_pool + w.s_head * kSlice;
   if (full) {
 #pragma unroll
-    for (int k = 0; k < kToks; ++k) cp_async_16(lane_dst + k * kPitch, src + (size_t)r[k] * stride);
+    for (int k = 0; k < kToks; ++k) cp_async_16(lane_dst + k * kPitch, src + (size_t)s.r[k] * stride);
   } else {
 #pragma unroll
     for (int k = 0; k < kToks; ++k)
-      cp_async_16_zfill(lane_dst + k * kPitch, src + (size_t)r[k] * stride, k < w.cnt ? 16u : 0u);
+      cp_async_16_zfill(lane_dst + k * kPitch, src + (size_t)s.r[k] * stride, k < w.cnt ? 16u : 0u);
   }
+}
+
+__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, const char* lane_pool,
+                                            uint32_t lane_dst, uint32_t stride, uint32_t max_row) {
+  StageRows s;
+  load_stage_rows(a, w, s);
+  copy_stage(a, w, s, lane_pool, lane_dst, stride, max_row);
 }
 
 template <int WARPS, int SLOTS>
@@ -311,14 +325,26 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
   const int share_begin = fc.pos;
   bool have_f = walk_next(sp, fc);
   int fslot = 0;
+  {
+    // the first stages' row indices are loaded together, then copied
+    Walk pw[SLOTS - 1];
+    StageRows pr[SLOTS - 1];
+    bool ph[SLOTS - 1];
 #pragma unroll
-  for (int s = 0; s < SLOTS - 1; ++s) {
-    if (have_f) {
-      issue_stage(a, fc, lane_pool, ring_dst + fslot * kSlotBytes, stride, max_row);
-      have_f = walk_next(sp, fc);
+    for (int s = 0; s < SLOTS - 1; ++s) {
+      ph[s] = have_f;
+      if (have_f) {
+        pw[s] = fc;
+        load_stage_rows(a, fc, pr[s]);
+        have_f = walk_next(sp, fc);
+      }
     }
-    cp_async_commit();
-    fslot = fslot + 1 == SLOTS ? 0 : fslot + 1;
+#pragma unroll
+    for (int s = 0; s < SLOTS - 1; ++s) {
+      if (ph[s]) copy_stage(a, pw[s], pr[s], lane_pool, ring_dst + fslot * kSlotBytes, stride, max_row);
+      cp_async_commit();
+      fslot = fslot + 1 == SLOTS ? 0 : fslot + 1;
+    }
   }
 
   uint32_t qb[8][2];
