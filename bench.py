@@ -433,9 +433,9 @@ def main() -> None:
 
     # ---- e2e: host (pinned) inputs copied in, every layer's output copied out, each step.
     # The copies run on their own streams (a step's inputs ahead of the step,
-    # into one of two buffer sets by step parity; each layer's output behind
-    # the layer that made it), ordered by events, so PCIe traffic overlaps the
-    # kernels.  The timed region spans every copy.
+    # into one of two buffer sets by step parity; the step's outputs behind
+    # it), ordered by events, so PCIe traffic overlaps the kernels.  The timed
+    # region spans every copy.
     qs, ks, vs = qkv
     hq, hk, hv = (t.cpu().pin_memory() for t in (qs, ks, vs))
     hout = torch.empty((n_layers, n_req, H * D), dtype=torch.bfloat16).pin_memory()
@@ -468,18 +468,17 @@ def main() -> None:
         b = batches[s]
         compute.wait_event(ready)
         backend.init_forward_metadata(b)
-        for layer in layers:
-            li = layer.layer_id
-            o = backend.forward(dq[li], dk[li], dv[li], layer, b)
-            made = torch.cuda.Event()
-            made.record(compute)
-            d2h.wait_event(made)
-            o.record_stream(d2h)
-            with torch.cuda.stream(d2h):
-                hout[li].copy_(o, non_blocking=True)
+        outs = [backend.forward(dq[layer.layer_id], dk[layer.layer_id], dv[layer.layer_id], layer, b)
+                for layer in layers]
         done = torch.cuda.Event()
         done.record(compute)
         step_done[s % 2] = done
+        # the step's outputs cross PCIe while the next step computes
+        d2h.wait_event(done)
+        with torch.cuda.stream(d2h):
+            for layer, o in zip(layers, outs, strict=True):
+                hout[layer.layer_id].copy_(o, non_blocking=True)
+                o.record_stream(d2h)
         if s + 1 < last:
             ready = copy_inputs(s + 1)  # the next step's inputs cross PCIe during this step
     compute.wait_stream(d2h)

@@ -239,6 +239,26 @@ int qq_sparse_decode_attention_noalloc(const qq_batch* batch, int top_k, const v
                                        int64_t kv_row_stride, int64_t num_rows, float scaling,
                                        void* out, int64_t out_stride, uint32_t* err, void* stream);
 
+/* ---- [Q5][Q6][Q7] + [Q7] selection and attention in one call ---------- */
+/* qq_quest_retrieve_topk (with the req_to_token translation into rows)
+ * followed by qq_sparse_decode_attention over those rows, q_heads x
+ * st->head_dim queries over st->kv_heads KV heads, both kernels sharing
+ * `workspace`.  The results are those of the two calls.  On the attention
+ * fast path the attention kernel starts while the selection still runs and
+ * reads a request's rows as soon as that request's ready word in the
+ * workspace holds this call's epoch (a per-call number the library keeps),
+ * so its set-up and the selection's tail overlap.  No reference
+ * counterpart: QuestOnlyBackend.forward_decode makes the two calls in turn
+ * (quest_only.py:153-158). */
+int qq_quest_decode_attention(const qq_quest_state* st, int layer, const qq_batch* batch,
+                              const void* q, int q_dtype, int q_heads, int64_t q_stride,
+                              int32_t* positions, int32_t* actual_lens, float* scores,
+                              const qq_token_table* translate, int32_t* rows,
+                              const qq_new_token* new_token, const void* k_pool, const void* v_pool,
+                              int64_t kv_row_stride, int64_t num_rows, float scaling, void* out,
+                              int64_t out_stride, uint32_t* err, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 /* ---- [H3] HiSparse swap-in -------------------------------------------- */
 /* For every request of the batch: fast path (seq_len <= buf: row = slot =
  * position) or first-occurrence dedupe, hit detection in LRU order,

@@ -121,6 +121,10 @@ SIGNATURES: dict[str, tuple] = {
     "qq_sparse_decode_attention": (
         c_int, [_B, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p,
                 c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "qq_quest_decode_attention": (
+        c_int, [_S, c_int, _B, c_void_p, c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p, _T, c_void_p,
+                _N, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p,
+                c_size_t, c_void_p]),
     "qq_sparse_decode_attention_noalloc": (
         c_int, [_B, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p,
                 c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p]),

@@ -133,6 +133,9 @@ class _QuestDecodeMixin:
         #: when a dict, every launch of the decode path records a (start, end)
         #: CUDA event pair under its kernel name (benchmark instrumentation)
         self.kernel_events: dict[str, list] | None = None
+        #: selection and attention in one call (qq_quest_decode_attention) when
+        #: nothing traces the selection or times the kernels one by one
+        self.fused = True
 
     def _ev_begin(self):
         if self.kernel_events is None:
@@ -280,6 +283,14 @@ class B200QuestOnlyBackend(_QuestDecodeMixin, AttentionBackend):
         dst = batch.out_cache_loc.to(device=self.device, dtype=torch.int64).contiguous()
         nt = self._new_token(kk, vv, k_buf, v_buf, dst, 0)
         table = _lib.QQTokenTable(self.req_to_token.data_ptr(), self.req_to_token.stride(0))
+        if self.fused and self.kernel_events is None and self.quest.trace is None:
+            # [Q6] + [Q7] selection, translation, new K/V write and attention in one call:
+            # the attention starts on each request as soon as its rows are written
+            out = torch.empty((bs, q3.shape[1] * q3.shape[2]), dtype=q3.dtype, device=self.device)
+            self.quest.select_attend(q3, li, reqs, seq, self._positions, self._actual, translate=table,
+                                     rows=self._rows, new_token=nt, k_pool=k_buf, v_pool=v_buf,
+                                     scaling=layer.scaling, out=out, err_ptr=self._attn_err.ptr())
+            return out
         # [Q6] + [Q7] translation + new K/V write, one launch
         ev = self._ev_begin()
         self.quest.select(q3, li, reqs, seq, self._positions, self._actual, translate=table,

@@ -30,6 +30,7 @@
 #include <cfloat>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -68,7 +69,35 @@ struct AttnArgs {
   uint32_t* err;
   float* part;        // [warps][2][kPartFloats]
   int32_t* seg_count; // [bs * kKV] arrival counters of split segments
+  // fused selection + attention: rows of request i may be read once
+  // ready[i] == epoch (the selection kernel runs ahead); null: the rows
+  // were written before this launch
+  const uint32_t* ready;
+  uint32_t epoch;
 };
+
+// Request r's rows are written: lane 0 spins on its ready word (acquire,
+// bounded), the warp barrier orders every lane's later reads after it.
+// `known` is the last request this warp saw ready (warps visit requests in
+// increasing order).
+__device__ __forceinline__ void ensure_ready(const AttnArgs& a, int r, int& known) {
+  if (a.ready == nullptr || r == known) return;
+  if ((threadIdx.x & 31) == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+      uint32_t v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.ready + r) : "memory");
+      if (v == a.epoch) break;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(a.err, QQ_DEV_ERR_TIMEOUT);
+        break;
+      }
+      __nanosleep(100);
+    }
+  }
+  __syncwarp();
+  known = r;
+}
 
 __device__ __forceinline__ void ldmatrix_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
                                             uint32_t addr) {
@@ -253,7 +282,8 @@ __device__ __forceinline__ void copy_stage(const AttnArgs& a, const Walk& w, Sta
 }
 
 __device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, const char* lane_pool,
-                                            uint32_t lane_dst, uint32_t stride, uint32_t max_row) {
+                                            uint32_t lane_dst, uint32_t stride, uint32_t max_row, int& known) {
+  ensure_ready(a, w.s_req, known);
   StageRows s;
   load_stage_rows(a, w, s);
   copy_stage(a, w, s, lane_pool, lane_dst, stride, max_row);
@@ -270,7 +300,9 @@ struct StreamCfg {
 template <int WARPS, int SLOTS>
 __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) {
   using Cfg = StreamCfg<WARPS, SLOTS>;
-  wait_prior_grid();
+  // behind a fused selection the ready words order the reads instead of the
+  // grid dependency; the selection's own wait keeps earlier grids ahead
+  if (a.ready == nullptr) wait_prior_grid();
   allow_next_grid();
   extern __shared__ __align__(128) char smem[];
   int32_t* s_prefix4 = reinterpret_cast<int32_t*>(smem + Cfg::kRing);
@@ -325,6 +357,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
   const int share_begin = fc.pos;
   bool have_f = walk_next(sp, fc);
   int fslot = 0;
+  int known = -1;  // the last request seen ready
   {
     // the first stages' row indices are loaded together, then copied
     Walk pw[SLOTS - 1];
@@ -335,6 +368,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       ph[s] = have_f;
       if (have_f) {
         pw[s] = fc;
+        ensure_ready(a, fc.s_req, known);
         load_stage_rows(a, fc, pr[s]);
         have_f = walk_next(sp, fc);
       }
@@ -370,7 +404,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
     cp_async_wait<SLOTS - 2>();
     __syncwarp();  // the current stage is visible to every lane; the previous stage's slot is free
     if (have_f) {
-      issue_stage(a, fc, lane_pool, ring_dst + fslot * kSlotBytes, stride, max_row);
+      issue_stage(a, fc, lane_pool, ring_dst + fslot * kSlotBytes, stride, max_row, known);
       have_f = walk_next(sp, fc);
     }
     cp_async_commit();
@@ -705,15 +739,18 @@ using namespace qq;
 
 extern "C" size_t qq_workspace_bytes(int max_bs, int top_k, int q_heads, int head_dim) {
   if (max_bs < 0 || top_k < 0 || q_heads < 0 || head_dim < 0) return 0;
-  return kPartialOffset + sizeof(float) * attn_partial_floats(sm_count()) + 256;
+  return workspace_end(sm_count()) + 256;
 }
 
-extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, int dtype,
-                                          int q_heads, int kv_heads, int head_dim, int64_t q_stride,
-                                          const int32_t* rows, const void* k_pool, const void* v_pool,
-                                          int64_t kv_row_stride, int64_t num_rows, float scaling,
-                                          void* out, int64_t out_stride, uint32_t* err, void* workspace,
-                                          size_t workspace_bytes, void* stream) {
+namespace qq {
+
+// qq_sparse_decode_attention; with `ready` the streaming kernel reads a
+// request's rows once ready[i] == epoch (see ensure_ready).
+int sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, int dtype, int q_heads,
+                            int kv_heads, int head_dim, int64_t q_stride, const int32_t* rows,
+                            const void* k_pool, const void* v_pool, int64_t kv_row_stride, int64_t num_rows,
+                            float scaling, void* out, int64_t out_stride, uint32_t* err, void* workspace,
+                            size_t workspace_bytes, void* stream, const uint32_t* ready, uint32_t epoch) {
   if (batch == nullptr || q == nullptr || rows == nullptr || k_pool == nullptr || v_pool == nullptr ||
       out == nullptr || top_k <= 0 || kv_heads <= 0 || head_dim <= 0 || q_heads % kv_heads != 0 ||
       num_rows <= 0)
@@ -750,7 +787,11 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
                     (out_stride % 2) == 0 && (reinterpret_cast<uintptr_t>(out) % 4) == 0 &&
                     (int64_t)batch->bs * top_k * kKV < (1ll << 31) && top_k % kToks == 0 &&
                     (reinterpret_cast<uintptr_t>(rows) % 16) == 0 && kv_row_stride * esz < (1ll << 32);
-  if (fast) return launch_stream(a, s);
+  if (fast) {
+    a.ready = ready;
+    a.epoch = epoch;
+    return launch_stream(a, s);
+  }
   const int G = q_heads / kv_heads;
   const size_t smem = sizeof(float) * ((size_t)G * head_dim + (size_t)G * top_k + 2 * (size_t)G);
   if (smem > 200 * 1024) return QQ_ERR_UNSUPPORTED;
@@ -769,6 +810,50 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
     attn_generic_kernel<float><<<grid, 128, smem, s>>>(a, q_heads, kv_heads, head_dim);
   }
   return launch_status();
+}
+
+int retrieve_topk(const qq_quest_state* st, int layer, const qq_batch* batch, const void* q, int q_dtype,
+                  int q_heads, int64_t q_stride, int32_t* positions, int32_t* actual_lens, float* scores,
+                  const qq_token_table* translate, int32_t* rows, const qq_new_token* nt, void* workspace,
+                  size_t workspace_bytes, void* stream, uint32_t* ready, uint32_t epoch);
+
+namespace {
+std::atomic<uint32_t> g_epoch{0};
+}  // namespace
+
+}  // namespace qq
+
+extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, int dtype,
+                                          int q_heads, int kv_heads, int head_dim, int64_t q_stride,
+                                          const int32_t* rows, const void* k_pool, const void* v_pool,
+                                          int64_t kv_row_stride, int64_t num_rows, float scaling,
+                                          void* out, int64_t out_stride, uint32_t* err, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  return qq::sparse_decode_attention(batch, top_k, q, dtype, q_heads, kv_heads, head_dim, q_stride, rows, k_pool,
+                                     v_pool, kv_row_stride, num_rows, scaling, out, out_stride, err, workspace,
+                                     workspace_bytes, stream, nullptr, 0);
+}
+
+extern "C" int qq_quest_decode_attention(const qq_quest_state* st, int layer, const qq_batch* batch,
+                                         const void* q, int q_dtype, int q_heads, int64_t q_stride,
+                                         int32_t* positions, int32_t* actual_lens, float* scores,
+                                         const qq_token_table* translate, int32_t* rows,
+                                         const qq_new_token* new_token, const void* k_pool,
+                                         const void* v_pool, int64_t kv_row_stride, int64_t num_rows,
+                                         float scaling, void* out, int64_t out_stride, uint32_t* err,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (st == nullptr || batch == nullptr || rows == nullptr || translate == nullptr) return QQ_ERR_INVALID;
+  if (workspace == nullptr || workspace_bytes < qq_workspace_bytes(batch->bs, st->top_k, q_heads, st->head_dim))
+    return QQ_ERR_WORKSPACE;
+  uint32_t epoch = ++g_epoch;
+  if (epoch == 0) epoch = ++g_epoch;  // 0 is a cleared word
+  uint32_t* ready = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + ready_offset(sm_count()));
+  int rc = retrieve_topk(st, layer, batch, q, q_dtype, q_heads, q_stride, positions, actual_lens, scores,
+                         translate, rows, new_token, workspace, workspace_bytes, stream, ready, epoch);
+  if (rc != QQ_OK) return rc;
+  return sparse_decode_attention(batch, st->top_k, q, q_dtype, q_heads, st->kv_heads, st->head_dim, q_stride,
+                                 rows, k_pool, v_pool, kv_row_stride, num_rows, scaling, out, out_stride, err,
+                                 workspace, workspace_bytes, stream, ready, epoch);
 }
 
 // ------------------------------------------------------------------ attention without a workspace

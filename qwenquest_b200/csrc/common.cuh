@@ -234,5 +234,10 @@ constexpr size_t kAttnPartialFloats = 2 * (8 * 128 + 2 * 8);
 inline size_t attn_partial_floats(int sm_count) {
   return (size_t)sm_count * kAttnWarpsPerSm * kAttnPartialFloats;
 }
+// Then one ready word per request (uint32) for the fused selection +
+// attention call: the selection stores the call's epoch once the request's
+// rows are written, the attention spins on it.
+inline size_t ready_offset(int sm_count) { return kPartialOffset + sizeof(float) * attn_partial_floats(sm_count); }
+inline size_t workspace_end(int sm_count) { return ready_offset(sm_count) + sizeof(uint32_t) * QQ_MAX_BS; }
 
 }  // namespace qq

@@ -60,7 +60,18 @@ struct SelectArgs {
   int units;      // bs * parts
   int score_all;  // page_scores API: score pages [0, num_pages) of every request, no selection
   int num_pages;
+  uint32_t* ready;  // optional: ready[i] = epoch once request i's positions and rows are written
+  uint32_t epoch;
 };
+
+// Request i's layout is written (by the whole block, before a barrier): its
+// ready word takes this launch's epoch, after a fence, for a consumer that
+// spins on it instead of waiting for the whole grid.
+__device__ __forceinline__ void publish_ready(const SelectArgs& a, int i) {
+  if (a.ready == nullptr) return;
+  __threadfence();
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.ready + i), "r"(a.epoch) : "memory");
+}
 
 // Dynamic shared memory of the selection: order keys of the candidate
 // pages, then the selected pages, their keys and their score order.
@@ -460,6 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
       __syncthreads();
       write_layout(a, i, req, L, is_long, sel, s_top);
       __syncthreads();  // s_lists and s_top are free again
+      if (tid == 0) publish_ready(a, i);
       continue;
     }
 
@@ -478,6 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     __syncthreads();
     if (s_last) select_request(a, i, req, L, C, is_long, s_dyn, s_hist, s_digit, s_above, s_ngt);
     __syncthreads();  // the selection's shared memory is free again
+    if (s_last && tid == 0) publish_ready(a, i);
   }
 }
 
@@ -567,12 +580,14 @@ void plan_units(SelectArgs& a, int pages, int bs, int* grid) {
 
 using namespace qq;
 
-extern "C" int qq_quest_retrieve_topk(const qq_quest_state* st, int layer, const qq_batch* batch,
-                                      const void* q, int q_dtype, int q_heads, int64_t q_stride,
-                                      int32_t* positions, int32_t* actual_lens, float* scores,
-                                      const qq_token_table* translate, int32_t* rows,
-                                      const qq_new_token* nt, void* workspace,
-                                      size_t workspace_bytes, void* stream) {
+namespace qq {
+
+// qq_quest_retrieve_topk, optionally publishing per-request ready words
+// (ready[i] = epoch) for a consumer launched behind it.
+int retrieve_topk(const qq_quest_state* st, int layer, const qq_batch* batch, const void* q, int q_dtype,
+                  int q_heads, int64_t q_stride, int32_t* positions, int32_t* actual_lens, float* scores,
+                  const qq_token_table* translate, int32_t* rows, const qq_new_token* nt, void* workspace,
+                  size_t workspace_bytes, void* stream, uint32_t* ready, uint32_t epoch) {
   if (!valid_state(st) || batch == nullptr || layer < 0 || layer >= st->num_layers) return QQ_ERR_INVALID;
   if (st->top_k <= 0 || st->top_k % st->page_size != 0) return QQ_ERR_INVALID;
   if (batch->bs == 0) return QQ_OK;
@@ -600,6 +615,8 @@ extern "C" int qq_quest_retrieve_topk(const qq_quest_state* st, int layer, const
   a.rows = rows;
   a.counters = ws_counters(workspace, kCounterSelect);
   a.lists = ws_select_lists(workspace);
+  a.ready = ready;
+  a.epoch = epoch;
   if (nt != nullptr && nt->k != nullptr) {
     const int esz = nt->dtype == QQ_F32 ? 4 : 2;
     const int64_t row_bytes = (int64_t)st->kv_heads * st->head_dim * esz;
@@ -626,6 +643,18 @@ extern "C" int qq_quest_retrieve_topk(const qq_quest_state* st, int layer, const
   const int kw = words_for(st->kv_heads * st->head_dim);
   if (q_dtype == QQ_BF16) return launch_select<__nv_bfloat16>(a, grid, kw, smem, s);
   return launch_select<float>(a, grid, kw, smem, s);
+}
+
+}  // namespace qq
+
+extern "C" int qq_quest_retrieve_topk(const qq_quest_state* st, int layer, const qq_batch* batch,
+                                      const void* q, int q_dtype, int q_heads, int64_t q_stride,
+                                      int32_t* positions, int32_t* actual_lens, float* scores,
+                                      const qq_token_table* translate, int32_t* rows,
+                                      const qq_new_token* nt, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  return qq::retrieve_topk(st, layer, batch, q, q_dtype, q_heads, q_stride, positions, actual_lens, scores,
+                           translate, rows, nt, workspace, workspace_bytes, stream, nullptr, 0);
 }
 
 extern "C" int qq_quest_group_queries(const void* q, int dtype, int bs, int q_heads, int kv_heads,

@@ -364,6 +364,23 @@ class QuestAlgorithm:
             self._record(layer_id, reqs, seq_lens, positions, scores)
         return scores
 
+    def select_attend(self, q, layer_id, reqs, seq_lens, positions, actual_lens, *, translate, rows,
+                      new_token, k_pool, v_pool, scaling, out, err_ptr, scores=None) -> None:
+        """One ``qq_quest_decode_attention`` call: ``select`` (with ``rows``) and the sparse
+        decode attention over those rows into ``out``, the attention kernel starting on each
+        request as soon as its rows are written.  Not traced (use ``select`` for traces)."""
+        bs = int(reqs.shape[0])
+        scores = self._scores_buf(bs) if scores is None else scores
+        batch = _lib.QQBatch(reqs.data_ptr(), seq_lens.data_ptr(), bs)
+        rc = self.lib.qq_quest_decode_attention(
+            self._state, layer_id - self.start_layer, batch, q.data_ptr(), dtype_code(q.dtype), q.shape[1],
+            q.stride(0), positions.data_ptr(), actual_lens.data_ptr() if actual_lens is not None else None,
+            scores.data_ptr(), translate, rows.data_ptr(), new_token, k_pool.data_ptr(), v_pool.data_ptr(),
+            k_pool.stride(0), k_pool.shape[0], float(scaling), out.data_ptr(), out.stride(0), err_ptr,
+            self._workspace.data_ptr(), self._workspace.numel(), self._stream(),
+        )
+        check(rc, "decode attention")
+
     # ------------------------------------------------------ [Q8] request end
 
     def invalidate_request(self, req_pool_idx: int) -> None:
