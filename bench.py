@@ -443,46 +443,49 @@ def main() -> None:
     compute = torch.cuda.current_stream(dev)
     h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for s in range(2 * total, 2 * total + args.warmup):
-        run_step(backend, batches[s], layers, qkv)
+
+    def e2e_steps(first, last):
+        """Steps [first, last) with their copies; returns with every stream's work queued."""
+        step_done = [None, None]  # compute finished with the buffer set of that parity
+
+        def copy_inputs(s):
+            if step_done[s % 2] is not None:
+                h2d.wait_event(step_done[s % 2])
+            with torch.cuda.stream(h2d):
+                for dst, src in zip(dbuf[s % 2], (hq, hk, hv), strict=True):
+                    dst.copy_(src, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(h2d)
+            return ev
+
+        h2d.wait_stream(compute)
+        d2h.wait_stream(compute)
+        ready = copy_inputs(first)
+        for s in range(first, last):
+            dq, dk, dv = dbuf[s % 2]
+            b = batches[s]
+            compute.wait_event(ready)
+            backend.init_forward_metadata(b)
+            outs = [backend.forward(dq[layer.layer_id], dk[layer.layer_id], dv[layer.layer_id], layer, b)
+                    for layer in layers]
+            done = torch.cuda.Event()
+            done.record(compute)
+            step_done[s % 2] = done
+            # the step's outputs cross PCIe while the next step computes
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                for layer, o in zip(layers, outs, strict=True):
+                    hout[layer.layer_id].copy_(o, non_blocking=True)
+                    o.record_stream(d2h)
+            if s + 1 < last:
+                ready = copy_inputs(s + 1)  # the next step's inputs cross PCIe during this step
+        compute.wait_stream(d2h)
+        compute.wait_stream(h2d)
+
+    e2e_steps(2 * total, 2 * total + args.warmup)  # warm-up: the same steps, copies included
     barrier()
     e2e_start.record(compute)
-    h2d.wait_event(e2e_start)
-    d2h.wait_event(e2e_start)
-    step_done = [None, None]  # compute finished with the buffer set of that parity
-
-    def copy_inputs(s):
-        if step_done[s % 2] is not None:
-            h2d.wait_event(step_done[s % 2])
-        with torch.cuda.stream(h2d):
-            for dst, src in zip(dbuf[s % 2], (hq, hk, hv), strict=True):
-                dst.copy_(src, non_blocking=True)
-        ev = torch.cuda.Event()
-        ev.record(h2d)
-        return ev
-
-    first, last = 2 * total + args.warmup, 3 * total
-    ready = copy_inputs(first)
-    for s in range(first, last):
-        dq, dk, dv = dbuf[s % 2]
-        b = batches[s]
-        compute.wait_event(ready)
-        backend.init_forward_metadata(b)
-        outs = [backend.forward(dq[layer.layer_id], dk[layer.layer_id], dv[layer.layer_id], layer, b)
-                for layer in layers]
-        done = torch.cuda.Event()
-        done.record(compute)
-        step_done[s % 2] = done
-        # the step's outputs cross PCIe while the next step computes
-        d2h.wait_event(done)
-        with torch.cuda.stream(d2h):
-            for layer, o in zip(layers, outs, strict=True):
-                hout[layer.layer_id].copy_(o, non_blocking=True)
-                o.record_stream(d2h)
-        if s + 1 < last:
-            ready = copy_inputs(s + 1)  # the next step's inputs cross PCIe during this step
-    compute.wait_stream(d2h)
-    compute.wait_stream(h2d)
+    e2e_steps(2 * total + args.warmup, 3 * total)
     e2e_end.record(compute)
     barrier()
     e2e_ms = e2e_start.elapsed_time(e2e_end)

@@ -278,8 +278,11 @@ __device__ void select_request(const SelectArgs& a, int i, int64_t req, int64_t 
   write_layout(a, i, req, L, is_long, sel, s_order);
 }
 
-// KW 16-byte words per lane and page, DEPTH pages in flight per warp.
-template <typename QT, int KW, int DEPTH>
+// KW 16-byte words per lane and page; pages in flight per warp: DEPTH in
+// registers, or with RING > 0 RING - 1 in a per-warp ring of RING page slots
+// in shared memory filled by cp.async (each lane copies and reads only its
+// own words, so the waits are per thread and no barrier is needed).
+template <typename QT, int KW, int DEPTH, int RING = 0>
 __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a) {
   constexpr int kQPerThread = QQ_MAX_CHANNELS / kThreads;  // query-mean channels per thread
   __shared__ float s_qbar[QQ_MAX_CHANNELS];
@@ -346,8 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     const uint4* bounds = reinterpret_cast<const uint4*>(st.page_bounds) +
                           ((size_t)a.layer * st.max_reqs + req) * st.max_pages * page_words;
 
-    // the first DEPTH pages of this warp in flight
-    uint4 buf[DEPTH][KW];
+    // the first DEPTH (RING - 1) pages of this warp in flight
+    uint4 buf[RING > 0 ? 1 : DEPTH][KW];
     auto load_page = [&](uint4 (&w)[KW], int64_t p) {
       const uint4* src = bounds + (size_t)p * page_words;
 #pragma unroll
@@ -357,9 +360,26 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
       }
     };
     const int64_t pw0 = pg0 + warp;
+    const int npages = p_end > pw0 ? (int)((p_end - pw0 + kWarps - 1) / kWarps) : 0;  // this warp's pages
+    constexpr uint32_t kSlot = KW * 32 * 16;  // bytes of one page
+    const uint32_t ring = smem_u32(s_dyn) + (uint32_t)warp * (RING > 0 ? RING : 1) * kSlot + lane * 16;
+    auto copy_page = [&](int slot, int64_t p) {
+      const uint4* src = bounds + (size_t)p * page_words;
 #pragma unroll
-    for (int d = 0; d < DEPTH; ++d)
-      if (pw0 + d * kWarps < p_end) load_page(buf[d], pw0 + d * kWarps);
+      for (int it = 0; it < KW; ++it)
+        if (lane + 32 * it < nvec) cp_async_16(ring + slot * kSlot + it * 512, src + lane + 32 * it);
+    };
+    if constexpr (RING > 0) {
+#pragma unroll
+      for (int d = 0; d < RING - 1; ++d) {
+        if (d < npages) copy_page(d, pw0 + (int64_t)d * kWarps);
+        cp_async_commit();
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < DEPTH; ++d)
+        if (pw0 + d * kWarps < p_end) load_page(buf[d], pw0 + d * kWarps);
+    }
 
     // (a) the new token's K/V into its pool row (quest_only.py:136-137, coordinator.py:226-228)
     if (a.nt_k != nullptr && j == 0) {
@@ -391,34 +411,61 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
           pick[it][e] = qv[it][e] >= 0.f ? 0x3244u : 0x1044u;  // high half (max) or low half (min)
         }
       }
-      for (int64_t pc = pw0; pc < p_end; pc += DEPTH * kWarps) {
+      // one page's score: every lane ends with the same value
+      auto page_score = [&](const uint4 (&w)[KW]) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int d = 0; d < DEPTH; ++d) {
-          const int64_t p = pc + d * kWarps;
-          if (p < p_end) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int it = 0; it < KW; ++it) {
+          acc[0] = bound_fma<QT>(qv[it][0], __uint_as_float(__byte_perm(w[it].x, 0u, pick[it][0])), acc[0]);
+          acc[1] = bound_fma<QT>(qv[it][1], __uint_as_float(__byte_perm(w[it].y, 0u, pick[it][1])), acc[1]);
+          acc[2] = bound_fma<QT>(qv[it][2], __uint_as_float(__byte_perm(w[it].z, 0u, pick[it][2])), acc[2]);
+          acc[3] = bound_fma<QT>(qv[it][3], __uint_as_float(__byte_perm(w[it].w, 0u, pick[it][3])), acc[3]);
+        }
+        return __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+      };
+      auto take_score = [&](float sum, int64_t p) {
+        // butterfly sum over the lanes
 #pragma unroll
-            for (int it = 0; it < KW; ++it) {
-              const uint4 w = buf[d][it];
-              acc[0] = bound_fma<QT>(qv[it][0], __uint_as_float(__byte_perm(w.x, 0u, pick[it][0])), acc[0]);
-              acc[1] = bound_fma<QT>(qv[it][1], __uint_as_float(__byte_perm(w.y, 0u, pick[it][1])), acc[1]);
-              acc[2] = bound_fma<QT>(qv[it][2], __uint_as_float(__byte_perm(w.z, 0u, pick[it][2])), acc[2]);
-              acc[3] = bound_fma<QT>(qv[it][3], __uint_as_float(__byte_perm(w.w, 0u, pick[it][3])), acc[3]);
-            }
-            // the next page of this slot goes in flight before the reduction
-            const int64_t pn = p + DEPTH * kWarps;
-            if (pn < p_end) load_page(buf[d], pn);
-            // butterfly sum: every lane ends with the same value
-            float sum = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+        for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        if (lane == 0) scores[p] = sum;
+        if (lists) {
+          const uint64_t key = composite_key(sum, p);
+          if (key > top_min) {
+            top32_insert(top, key, lane);
+            top_min = shfl64(top, 31);
+          }
+        }
+      };
+      if constexpr (RING > 0) {
+        for (int k = 0; k < npages; ++k) {
+          cp_async_wait<RING - 2>();  // page k is in its slot
+          const int kn = k + RING - 1;
+          if (kn < npages) copy_page(kn % RING, pw0 + (int64_t)kn * kWarps);
+          cp_async_commit();
+          uint4 w[KW];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-            if (lane == 0) scores[p] = sum;
-            if (lists) {
-              const uint64_t key = composite_key(sum, p);
-              if (key > top_min) {
-                top32_insert(top, key, lane);
-                top_min = shfl64(top, 31);
-              }
+          for (int it = 0; it < KW; ++it) {
+            const uint32_t addr = ring + (k % RING) * kSlot + it * 512;
+            if (lane + 32 * it < nvec)
+              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(w[it].x), "=r"(w[it].y), "=r"(w[it].z), "=r"(w[it].w)
+                           : "r"(addr));
+            else
+              w[it] = make_uint4(0, 0, 0, 0);
+          }
+          take_score(page_score(w), pw0 + (int64_t)k * kWarps);
+        }
+      } else {
+        for (int64_t pc = pw0; pc < p_end; pc += DEPTH * kWarps) {
+#pragma unroll
+          for (int d = 0; d < DEPTH; ++d) {
+            const int64_t p = pc + d * kWarps;
+            if (p < p_end) {
+              const float sum = page_score(buf[d]);
+              // the next page of this slot goes in flight before the reduction
+              const int64_t pn = p + DEPTH * kWarps;
+              if (pn < p_end) load_page(buf[d], pn);
+              take_score(sum, p);
             }
           }
         }
@@ -514,31 +561,42 @@ int words_for(int nch) {
   return nvec <= 32 ? 1 : nvec <= 64 ? 2 : nvec <= 128 ? 4 : 8;  // nch <= QQ_MAX_CHANNELS = 1024
 }
 
+// Page slots of the shared-memory ring of the 4-word (512-channel) kernel:
+// 5 pages (10 KiB) in flight per warp, 160 KiB per block.
+constexpr int kRing4 = 6;
+
 template <typename QT>
 const void* kernel_for(int kw) {
   switch (kw) {
     case 1: return (const void*)score_select_kernel<QT, 1, 4>;
     case 2: return (const void*)score_select_kernel<QT, 2, 4>;
-    case 4: return (const void*)score_select_kernel<QT, 4, 3>;
+    case 4: return (const void*)score_select_kernel<QT, 4, 1, kRing4>;
     default: return (const void*)score_select_kernel<QT, 8, 1>;
   }
 }
 
+// Dynamic shared memory of the kernel for kw words per lane: the selection's
+// buffers, or the ring (they are never in use together).
+inline size_t select_dyn_smem(int kw, size_t selection) {
+  const size_t ring = kw == 4 ? (size_t)kWarps * kRing4 * 4 * 32 * 16 : 0;
+  return selection > ring ? selection : ring;
+}
+
 template <typename QT>
 int launch_select(const SelectArgs& a, int grid, int kw, size_t smem, cudaStream_t s) {
-  static size_t attr_smem = 48 * 1024;  // the default limit
-  if (smem > attr_smem) {
-    const int kws[4] = {1, 2, 4, 8};
-    for (int k : kws)
-      if (cudaFuncSetAttribute(kernel_for<QT>(k), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-          cudaSuccess)
-        return QQ_ERR_CUDA;
-    attr_smem = smem;
+  static size_t attr_smem[4] = {48 * 1024, 48 * 1024, 48 * 1024, 48 * 1024};  // the default limit
+  const int ki = kw == 1 ? 0 : kw == 2 ? 1 : kw == 4 ? 2 : 3;
+  smem = select_dyn_smem(kw, smem);
+  if (smem > attr_smem[ki]) {
+    if (cudaFuncSetAttribute(kernel_for<QT>(kw), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return QQ_ERR_CUDA;
+    attr_smem[ki] = smem;
   }
   switch (kw) {
     case 1: return launch_pdl(score_select_kernel<QT, 1, 4>, dim3(grid), dim3(kThreads), smem, s, a);
     case 2: return launch_pdl(score_select_kernel<QT, 2, 4>, dim3(grid), dim3(kThreads), smem, s, a);
-    case 4: return launch_pdl(score_select_kernel<QT, 4, 3>, dim3(grid), dim3(kThreads), smem, s, a);
+    case 4: return launch_pdl(score_select_kernel<QT, 4, 1, kRing4>, dim3(grid), dim3(kThreads), smem, s, a);
     default: return launch_pdl(score_select_kernel<QT, 8, 1>, dim3(grid), dim3(kThreads), smem, s, a);
   }
 }
