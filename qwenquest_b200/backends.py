@@ -128,6 +128,10 @@ class _QuestDecodeMixin:
         self._attn_err = _DeviceError(torch.zeros(1, dtype=torch.int32).pin_memory())
         self._step_reqs: torch.Tensor | None = None
         self._step_seq: torch.Tensor | None = None
+        self._step_dst: torch.Tensor | None = None
+        self._step_loc_src = None
+        self._step_batch = None
+        self._r2t_table = None
         self._max_reqs = max_reqs
         self.lib = _lib.load()
         #: when a dict, every launch of the decode path records a (start, end)
@@ -155,6 +159,19 @@ class _QuestDecodeMixin:
         self._step_reqs = batch.req_pool_indices.to(device=self.device, dtype=torch.int64).contiguous()
         self._step_seq = batch.seq_lens.to(device=self.device, dtype=torch.int64).contiguous()
         self.quest.prepare_step(self._step_seq)
+        # per-step constants of every layer's launch, built once
+        loc = getattr(batch, "out_cache_loc", None)
+        self._step_dst = None if loc is None else loc.to(device=self.device, dtype=torch.int64).contiguous()
+        self._step_loc_src = loc
+        self._step_batch = _lib.QQBatch(self._step_reqs.data_ptr(), self._step_seq.data_ptr(),
+                                        int(self._step_reqs.shape[0]))
+
+    def _token_table(self) -> _lib.QQTokenTable:
+        r2t = self.req_to_token
+        t = self._r2t_table
+        if t is None or t.req_to_token != r2t.data_ptr() or t.stride != r2t.stride(0):
+            t = self._r2t_table = _lib.QQTokenTable(r2t.data_ptr(), r2t.stride(0))
+        return t
 
     def check_errors(self) -> None:
         """Raise for device errors reported by earlier launches (no synchronisation)."""
@@ -280,16 +297,19 @@ class B200QuestOnlyBackend(_QuestDecodeMixin, AttentionBackend):
         q3 = self._q3(q, bs)
         kk = k.to(k_buf.dtype).reshape(bs, -1).contiguous()
         vv = v.to(v_buf.dtype).reshape(bs, -1).contiguous()
-        dst = batch.out_cache_loc.to(device=self.device, dtype=torch.int64).contiguous()
+        dst = self._step_dst
+        if dst is None or dst.shape[0] != bs or batch.out_cache_loc is not getattr(self, "_step_loc_src", None):
+            dst = batch.out_cache_loc.to(device=self.device, dtype=torch.int64).contiguous()
         nt = self._new_token(kk, vv, k_buf, v_buf, dst, 0)
-        table = _lib.QQTokenTable(self.req_to_token.data_ptr(), self.req_to_token.stride(0))
+        table = self._token_table()
         if self.fused and self.kernel_events is None and self.quest.trace is None:
             # [Q6] + [Q7] selection, translation, new K/V write and attention in one call:
             # the attention starts on each request as soon as its rows are written
             out = torch.empty((bs, q3.shape[1] * q3.shape[2]), dtype=q3.dtype, device=self.device)
             self.quest.select_attend(q3, li, reqs, seq, self._positions, self._actual, translate=table,
                                      rows=self._rows, new_token=nt, k_pool=k_buf, v_pool=v_buf,
-                                     scaling=layer.scaling, out=out, err_ptr=self._attn_err.ptr())
+                                     scaling=layer.scaling, out=out, err_ptr=self._attn_err.ptr(),
+                                     batch=self._step_batch)
             return out
         # [Q6] + [Q7] translation + new K/V write, one launch
         ev = self._ev_begin()

@@ -369,9 +369,14 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
       for (int it = 0; it < KW; ++it)
         if (lane + 32 * it < nvec) cp_async_16(ring + slot * kSlot + it * 512, src + lane + 32 * it);
     };
+    // With the ring one page per warp goes in flight before the query
+    // loads are used, the others once q̄ is in registers: a deeper start
+    // queues the query loads of every block behind the pages and delays the
+    // first scores (measured).
+    constexpr int kPre = 1;
     if constexpr (RING > 0) {
 #pragma unroll
-      for (int d = 0; d < RING - 1; ++d) {
+      for (int d = 0; d < kPre; ++d) {
         if (d < npages) copy_page(d, pw0 + (int64_t)d * kWarps);
         cp_async_commit();
       }
@@ -398,6 +403,13 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
       for (int ci = 0; ci < kQPerThread; ++ci) {
         const int c = tid + ci * kThreads;
         if (c < nch) s_qbar[c] = G == 1 ? qsum[ci] : Elem<QT>::round(__fdiv_rn(qsum[ci], (float)G));
+      }
+      if constexpr (RING > 0) {
+#pragma unroll
+        for (int d = kPre; d < RING - 1; ++d) {
+          if (d < npages) copy_page(d, pw0 + (int64_t)d * kWarps);
+          cp_async_commit();
+        }
       }
       __syncthreads();
       float qv[KW][4];

@@ -365,13 +365,14 @@ class QuestAlgorithm:
         return scores
 
     def select_attend(self, q, layer_id, reqs, seq_lens, positions, actual_lens, *, translate, rows,
-                      new_token, k_pool, v_pool, scaling, out, err_ptr, scores=None) -> None:
+                      new_token, k_pool, v_pool, scaling, out, err_ptr, scores=None, batch=None) -> None:
         """One ``qq_quest_decode_attention`` call: ``select`` (with ``rows``) and the sparse
         decode attention over those rows into ``out``, the attention kernel starting on each
         request as soon as its rows are written.  Not traced (use ``select`` for traces)."""
         bs = int(reqs.shape[0])
         scores = self._scores_buf(bs) if scores is None else scores
-        batch = _lib.QQBatch(reqs.data_ptr(), seq_lens.data_ptr(), bs)
+        if batch is None:
+            batch = _lib.QQBatch(reqs.data_ptr(), seq_lens.data_ptr(), bs)
         rc = self.lib.qq_quest_decode_attention(
             self._state, layer_id - self.start_layer, batch, q.data_ptr(), dtype_code(q.dtype), q.shape[1],
             q.stride(0), positions.data_ptr(), actual_lens.data_ptr() if actual_lens is not None else None,
