@@ -550,71 +550,63 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
     auto rec_of = [&](int r) -> const float* {
       return a.part + ((int64_t)(w_first + r) * 2 + (r == 0 ? first_slot : 0)) * kPartFloats;
     };
-    // (m, l) of this lane's head, eight records at a time: running max M and sum S
-    constexpr int kMB = 8;
+    // one pass over the records, two at a time: every lane's 32 channels
+    // and its head's (m, l) of each are in flight together, and a running
+    // max M rescales the sums as it grows
+    constexpr int kOB = 2;
+    const int c0 = (lane & 3) * 32;
     float M = kNegInf, S = 0.f;
-    for (int r0 = 0; r0 < nrec; r0 += kMB) {
-      float2 ml[kMB];
+    float o[32];
 #pragma unroll
-      for (int j = 0; j < kMB; ++j)
-        ml[j] = r0 + j < nrec ? __ldcg(reinterpret_cast<const float2*>(rec_of(r0 + j) + kG * kD + hq * 2))
-                              : make_float2(kNegInf, 0.f);
+    for (int e = 0; e < 32; ++e) o[e] = 0.f;
+    for (int r0 = 0; r0 < nrec; r0 += kOB) {
+      float2 ml[kOB];
+      float4 x[kOB][8];
+#pragma unroll
+      for (int j = 0; j < kOB; ++j) {
+        if (r0 + j < nrec) {
+          const float* rw = rec_of(r0 + j);
+          ml[j] = __ldcg(reinterpret_cast<const float2*>(rw + kG * kD + hq * 2));
+          const float4* src = reinterpret_cast<const float4*>(rw + hq * kD + c0);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) x[j][v] = __ldcg(src + v);
+        } else {
+          ml[j] = make_float2(kNegInf, 0.f);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) x[j][v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
       float Mb = M;
 #pragma unroll
-      for (int j = 0; j < kMB; ++j) Mb = fmaxf(Mb, ml[j].x);
-      if (Mb != kNegInf) {
-        S *= fast_exp2(M - Mb);
+      for (int j = 0; j < kOB; ++j) Mb = fmaxf(Mb, ml[j].x);
+      if (Mb == kNegInf) continue;
+      const float sc = fast_exp2(M - Mb);  // 0 while M is -inf (S and o are 0 then)
+      S *= sc;
 #pragma unroll
-        for (int j = 0; j < kMB; ++j) S += ml[j].x == kNegInf ? 0.f : ml[j].y * fast_exp2(ml[j].x - Mb);
+      for (int e = 0; e < 32; ++e) o[e] *= sc;
+#pragma unroll
+      for (int j = 0; j < kOB; ++j) {
+        const float f = ml[j].x == kNegInf ? 0.f : fast_exp2(ml[j].x - Mb);
+        S += f * ml[j].y;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          o[4 * v] += f * x[j][v].x;
+          o[4 * v + 1] += f * x[j][v].y;
+          o[4 * v + 2] += f * x[j][v].z;
+          o[4 * v + 3] += f * x[j][v].w;
+        }
       }
       M = Mb;
     }
     const float inv = 1.f / S;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)cc.s_req * a.out_stride +
+                         (cc.s_head * kG + hq) * kD + c0;
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const int c0 = (lane & 3) * 32 + hf * 16;
-      float o[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) o[e] = 0.f;
-      constexpr int kOB = 4;  // records whose 16 channels are in flight together
-      for (int r0 = 0; r0 < nrec; r0 += kOB) {
-        float mr[kOB];
-        float4 x[kOB][4];
-#pragma unroll
-        for (int j = 0; j < kOB; ++j) {
-          if (r0 + j < nrec) {
-            const float* rw = rec_of(r0 + j);
-            mr[j] = __ldcg(rw + kG * kD + hq * 2);
-            const float4* src = reinterpret_cast<const float4*>(rw + hq * kD + c0);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) x[j][v] = __ldcg(src + v);
-          } else {
-            mr[j] = kNegInf;
-#pragma unroll
-            for (int v = 0; v < 4; ++v) x[j][v] = make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < kOB; ++j) {
-          const float f = mr[j] == kNegInf ? 0.f : fast_exp2(mr[j] - M);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            o[4 * v] += f * x[j][v].x;
-            o[4 * v + 1] += f * x[j][v].y;
-            o[4 * v + 2] += f * x[j][v].z;
-            o[4 * v + 3] += f * x[j][v].w;
-          }
-        }
-      }
-      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)cc.s_req * a.out_stride +
-                           (cc.s_head * kG + hq) * kD + c0;
-#pragma unroll
-      for (int e = 0; e < 16; e += 2) {
-        __nv_bfloat162 pr;
-        pr.x = __float2bfloat16_rn(o[e] * inv);
-        pr.y = __float2bfloat16_rn(o[e + 1] * inv);
-        *reinterpret_cast<__nv_bfloat162*>(out + e) = pr;
-      }
+    for (int e = 0; e < 32; e += 2) {
+      __nv_bfloat162 pr;
+      pr.x = __float2bfloat16_rn(o[e] * inv);
+      pr.y = __float2bfloat16_rn(o[e + 1] * inv);
+      *reinterpret_cast<__nv_bfloat162*>(out + e) = pr;
     }
   }
   cp_async_wait<0>();
