@@ -311,6 +311,15 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     const int64_t req = a.reqs[i];
     const int64_t L = a.score_all ? 0 : a.seq_lens[i];
     const QT* q = static_cast<const QT*>(a.q) + (int64_t)i * a.q_stride;
+    // the new token's K/V words (part 0 writes them to the pool row below):
+    // loaded here, with the query rows, so that their latency overlaps
+    const bool nt_here = a.nt_k != nullptr && j == 0;
+    const int64_t nt_dst_row = nt_here && a.nt_dst_rows != nullptr ? a.nt_dst_rows[i] : -1;
+    uint32_t nt_kw = 0, nt_vw = 0;
+    if (nt_here && tid < a.nt_row_words) {
+      nt_kw = a.nt_k[i * a.nt_src_stride_words + tid];
+      nt_vw = a.nt_v[i * a.nt_src_stride_words + tid];
+    }
     float qsum[kQPerThread];
 #pragma unroll
     for (int ci = 0; ci < kQPerThread; ++ci) {
@@ -387,12 +396,18 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     }
 
     // (a) the new token's K/V into its pool row (quest_only.py:136-137, coordinator.py:226-228)
-    if (a.nt_k != nullptr && j == 0) {
+    if (nt_here) {
       const int64_t b = a.nt_buf;
-      const int64_t dst = a.nt_dst_rows != nullptr ? a.nt_dst_rows[i] : req * (b + 1) + (L - 1 < b ? L - 1 : b);
-      for (int w = tid; dst >= 0 && dst < a.nt_dst_num_rows && w < a.nt_row_words; w += kThreads) {
-        a.nt_k_dst[dst * a.nt_dst_stride_words + w] = a.nt_k[i * a.nt_src_stride_words + w];
-        a.nt_v_dst[dst * a.nt_dst_stride_words + w] = a.nt_v[i * a.nt_src_stride_words + w];
+      const int64_t dst = a.nt_dst_rows != nullptr ? nt_dst_row : req * (b + 1) + (L - 1 < b ? L - 1 : b);
+      if (dst >= 0 && dst < a.nt_dst_num_rows) {
+        if (tid < a.nt_row_words) {
+          a.nt_k_dst[dst * a.nt_dst_stride_words + tid] = nt_kw;
+          a.nt_v_dst[dst * a.nt_dst_stride_words + tid] = nt_vw;
+        }
+        for (int w = tid + kThreads; w < a.nt_row_words; w += kThreads) {
+          a.nt_k_dst[dst * a.nt_dst_stride_words + w] = a.nt_k[i * a.nt_src_stride_words + w];
+          a.nt_v_dst[dst * a.nt_dst_stride_words + w] = a.nt_v[i * a.nt_src_stride_words + w];
+        }
       }
     }
 
