@@ -8,7 +8,8 @@ rows behind that request's ready word), so every decode output must be
 bit-identical to the two-call run of the same scenario: ragged lengths,
 dense fallbacks, requests that finish and admit new ones mid-run, and
 enough requests that the selection splits requests into parts and the
-attention splits segments across warps and blocks.
+attention splits segments across warps and blocks, and a batch of more
+requests than the GPU has SMs (dense and sparse mixed).
 """
 
 from __future__ import annotations
@@ -32,7 +33,17 @@ WIDE = Scenario(
 )
 
 
-@pytest.mark.parametrize("sc", [CONFIG2_SAMPLE, WIDE], ids=["config2", "wide"])
+_rng2 = np.random.default_rng(12)
+MANY = Scenario(
+    name="fused_many", layers=1, q_heads=32, kv_heads=4, head_dim=128, bf16=True,
+    top_k=2048, page_size=64, device_buffer_size=4096,
+    prompt_lens=tuple(int(x) for x in _rng2.integers(300, 3000, size=160)),
+    new_tokens=tuple(int(x) for x in _rng2.integers(2, 4, size=160)),
+    max_running=160, max_context_len=3072, seed=6, planted_pages=1, q_decode_only=True,
+)
+
+
+@pytest.mark.parametrize("sc", [CONFIG2_SAMPLE, WIDE, MANY], ids=["config2", "wide", "many"])
 def test_fused_call_equals_two_calls(sc, cuda_device):
     two = LifecycleDriver(sc, "quest", b200_api(), cuda_device, prefill="direct", trace=True)
     rec_two = two.run()
