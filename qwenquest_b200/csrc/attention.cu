@@ -693,6 +693,7 @@ namespace {
 
 template <int WARPS, int SLOTS>
 int launch_stream_variant(const AttnArgs& a, cudaStream_t s) {
+  static_assert(WARPS <= kAttnWarpsPerSm, "the workspace holds partial records for kAttnWarpsPerSm warps per SM");
   using Cfg = StreamCfg<WARPS, SLOTS>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -704,25 +705,9 @@ int launch_stream_variant(const AttnArgs& a, cudaStream_t s) {
   return launch_pdl(attn_stream_kernel<WARPS, SLOTS>, dim3(sm_count()), dim3(Cfg::kThreads), Cfg::kSmem, s, a);
 }
 
-// Warps per block x ring slots per warp.  QQ_ATTN_VARIANT (e.g. "12x2") picks
-// another instantiation for tuning sweeps; the default is the measured best.
-int launch_stream(const AttnArgs& a, cudaStream_t s) {
-  static int variant = -1;
-  if (variant < 0) {
-    const char* v = getenv("QQ_ATTN_VARIANT");
-    variant = 0;
-    if (v != nullptr) {
-      if (!strcmp(v, "8x3")) variant = 1;
-      else if (!strcmp(v, "12x2")) variant = 2;
-      else if (!strcmp(v, "6x4")) variant = 3;
-    }
-  }
-  switch (variant) {
-    case 2: return launch_stream_variant<12, 2>(a, s);
-    case 3: return launch_stream_variant<6, 4>(a, s);
-    default: return launch_stream_variant<8, 3>(a, s);
-  }
-}
+// 8 warps per block x 3 ring slots per warp: the measured best of the
+// variants tried (6 x 4, 12 x 2, 16 x 1).
+int launch_stream(const AttnArgs& a, cudaStream_t s) { return launch_stream_variant<8, 3>(a, s); }
 
 }  // namespace
 }  // namespace qq

@@ -228,8 +228,8 @@ inline uint64_t* ws_select_lists(void* ws) {
 constexpr size_t kPartialOffset = kSelectListOffset + kSelectListBytes;
 
 // Attention partials: two (m, l, O) records of 8 query heads x 128 channels
-// per warp of the streaming grid (at most 16 warps per SM).
-constexpr int kAttnWarpsPerSm = 16;  // upper bound over the streaming kernel variants
+// per warp of the streaming grid (8 warps per SM).
+constexpr int kAttnWarpsPerSm = 8;  // warps per block of the streaming kernel
 constexpr size_t kAttnPartialFloats = 2 * (8 * 128 + 2 * 8);
 inline size_t attn_partial_floats(int sm_count) {
   return (size_t)sm_count * kAttnWarpsPerSm * kAttnPartialFloats;
