@@ -519,6 +519,14 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
       }
       top = s_lists[cur][0][lane];
       if (a.parts > 1) {
+        // the req_to_token entries of this part's top pages go to L2 while
+        // the parts arrive, for the last one's translation
+        if (warp == 0 && a.r2t != nullptr && is_long && top != 0) {
+          const int64_t page = (int64_t)(0xFFFFFFFFu - (uint32_t)(top & 0xFFFFFFFFu));
+          const char* src = reinterpret_cast<const char*>(a.r2t + req * a.r2t_stride + page * st.page_size);
+          for (int off = 0; off < 4 * st.page_size; off += 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(src + off));
+        }
         // publish the part's list; the barrier and thread 0's fence order
         // every thread's writes before the arrival, the last arriver's fence
         // orders its reads after it
