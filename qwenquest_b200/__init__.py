@@ -7,7 +7,8 @@ Drop-in attention backends for the reference's ``Engine``:
 
 plus :class:`~qwenquest_b200.quest.QuestAlgorithm` and
 :class:`~qwenquest_b200.hisparse.HiSparseCoordinator` with the reference's
-APIs.  All decode work runs in hand-written CUDA kernels in ``libqquest.so``
+APIs, and :class:`~qwenquest_b200.graphs.DecodeStepGraph` (a decode step
+captured in a CUDA graph).  All decode work runs in hand-written CUDA kernels in ``libqquest.so``
 (C ABI: ``include/qquest.h``); nothing falls back to the CPU.  Importing this
 package does not load the library; the first backend / algorithm object does.
 """
@@ -17,6 +18,7 @@ __version__ = "0.1.0"
 __all__ = [
     "B200QuestHiSparseBackend",
     "B200QuestOnlyBackend",
+    "DecodeStepGraph",
     "HiSparseCoordinator",
     "QuestAlgorithm",
     "QuestTrace",
@@ -28,6 +30,10 @@ def __getattr__(name):
         from qwenquest_b200 import backends
 
         return getattr(backends, name)
+    if name == "DecodeStepGraph":
+        from qwenquest_b200.graphs import DecodeStepGraph
+
+        return DecodeStepGraph
     if name == "HiSparseCoordinator":
         from qwenquest_b200.hisparse import HiSparseCoordinator
 
