@@ -11,14 +11,16 @@
 //   written straight to the output; only the first and last segment of a
 //   share can be split, so a warp writes at most two fp32 partials
 //   (m, l, O), and the last warp to finish a split segment (an arrival
-//   counter in the workspace) merges it.
+//   counter in the workspace) merges it.  Behind a fused selection the
+//   kernel starts early and reads a request's rows once its ready word holds
+//   the call's epoch.
 // * Data movement: a warp gathers only its own KV head's 256-byte K and V
 //   slices.  Per 16-row stage every lane reads the stage's 16 row indices
 //   (four broadcast int4 loads) and issues 16 16-byte cp.async copies (one
 //   commit group per stage) into a private ring of slots at a 272-byte row
 //   pitch (ldmatrix reads are bank-conflict free).  Waits are per warp
 //   (cp.async.wait_group): no block barrier in the loop.  Warps per block x
-//   slots per warp are template parameters (8 x 3 by default).
+//   slots per warp are template parameters (8 x 3).
 // * Math per stage:
 //     S^T[16 rows x 8 heads] = K[16 x 128] . Q^T[128 x 8]   (8 x mma m16n8k16)
 //     online softmax in fp32 (exp2 domain), P^T via movmatrix.trans

@@ -5,18 +5,20 @@
 // a stride of the grid.  A unit is one part of one request's pages: with a
 // small batch a request is split into `parts` page ranges so that every SM
 // streams bounds.  Within a unit each warp streams its own pages (page
-// pg0 + warp + 16 m) straight into registers: lane l takes 16-byte words
-// l, l + 32, ... of a page (four channels' (min, max) pairs each) so that
-// its q̄ values stay in registers, the sign of q̄ picks max or min by a byte
-// permute, and DEPTH pages per warp are in flight while the warp reduces an
-// earlier one.  There is no block barrier inside a unit: the only ones are
-// around q̄ (computed once per unit, while the first pages are in flight)
-// and the unit's end, where the block arrives on the request's counter in
-// the workspace.  The last part of a request to arrive selects the top pages
-// from the fp32 scores (L2-resident by then): an 8-bit-per-pass radix
-// select of the sel-th largest score, ties to the lower pages, a rank sort of
-// the selected pages, then the position layout with the req_to_token reads
-// in flight together.
+// pg0 + warp + 16 m): lane l takes 16-byte words l, l + 32, ... of a page
+// (four channels' (min, max) pairs each) so that its q̄ values stay in
+// registers, and the sign of q̄ picks max or min by a byte permute.  For
+// 512 channels the pages pass through a per-warp ring of RING slots in
+// shared memory (cp.async, RING - 1 pages in flight); other widths load
+// DEPTH pages per warp into registers.  There is no block barrier inside a
+// unit: the only ones are around q̄ (computed once per unit, while the first
+// pages are in flight) and the unit's end, where each warp's running top 32
+// joins a merge tree and the block arrives on the request's counter in the
+// workspace.  The last part of a request to arrive merges the parts' lists
+// (or, beyond 32 selected pages, runs an 8-bit-per-pass radix select over
+// the fp32 scores), then writes the position layout with the req_to_token
+// reads in flight together; in a fused selection + attention call it then
+// marks the request ready.
 
 #include <type_traits>
 
