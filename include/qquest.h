@@ -150,6 +150,53 @@ int qq_quest_bounds_prefill(const qq_quest_state* st, int layer_begin, int layer
                             const int32_t* prefill_indices, int prefill_len, int req_pool_idx,
                             int write_counters, void* stream);
 
+/* ---- [Q2] + [H1] one prefill layer: K/V write, bounds, hot buffer ------ */
+/* An extend batch (ForwardBatch in EXTEND mode, batch.py:38-64): request i
+ * adds seq_lens[i] - prefix_lens[i] new tokens after prefix_lens[i] tokens
+ * already in the pool; its new tokens are rows token_offsets[i] .. of k, v
+ * and out_cache_loc. */
+typedef struct qq_extend_batch {
+  const int64_t* req_pool_indices; /* device [bs] */
+  const int64_t* seq_lens;         /* device [bs]: prefix + new tokens */
+  const int64_t* prefix_lens;      /* device [bs] (extend_prefix_lens) */
+  const int64_t* token_offsets;    /* device [bs]: first new-token row of request i */
+  const int64_t* out_cache_loc;    /* device [tokens]: pool row of each new token */
+  int64_t num_tokens;              /* rows of k, v and out_cache_loc; rows past it are skipped */
+  int32_t bs;
+  int32_t max_seq_len;             /* >= every seq_lens[i]; sizes the grid */
+} qq_extend_batch;
+
+/* The HiSparse device tier of one layer (coordinator.py:120-128): position
+ * pos < device_buffer_size of request req lives in row req * (buf + 1) + pos. */
+typedef struct qq_hot_buffer {
+  void* k;
+  void* v;
+  int64_t row_stride;         /* elements between rows */
+  int64_t device_buffer_size; /* buf */
+  int64_t num_rows;           /* rows of k / v; rows outside are skipped and reported */
+} qq_hot_buffer;
+
+/* One layer of an extend batch in one launch: the new tokens' K/V rows go
+ * to k_pool / v_pool at out_cache_loc (set_kv_buffer, memory.py:114-120);
+ * when st is given, layer `layer` of st gets the page bounds of positions
+ * [0, seq_len) of every request (full pages into page_bounds, a partial tail
+ * into the running bounds, counters written when write_counters != 0), as
+ * QuestAlgorithm.update_prefill_representations (quest.py:231-280) computes
+ * them after the last layer (QuestOnlyBackend._update_quest_for_extend,
+ * quest_only.py:101-128); when hot is given, positions [0, buf) are copied
+ * into the hot buffer, the device half of HiSparseCoordinator.admit_request
+ * (coordinator.py:154-162).  Keys and values of positions below a request's
+ * prefix come from the pool through table.  k / v: device
+ * [tokens][row_elems] rows src_stride elements apart, in the pool dtype.
+ * Rows and pointers 16-byte aligned use 16-byte moves, 4-byte aligned ones
+ * 4-byte moves, anything else returns QQ_ERR_UNSUPPORTED.  Out-of-range rows
+ * are skipped and set QQ_DEV_ERR_BOUNDS in err (nullable). */
+int qq_quest_extend_kv(const qq_quest_state* st, int layer, int write_counters,
+                       const qq_extend_batch* batch, const qq_token_table* table, const void* k,
+                       const void* v, int dtype, int64_t row_elems, int64_t src_stride, void* k_pool,
+                       void* v_pool, int64_t pool_row_stride, int64_t pool_rows, const qq_hot_buffer* hot,
+                       uint32_t* err, void* stream);
+
 /* ---- [Q3] per-step bounds fold + finalize ----------------------------- */
 #define QQ_STEP_FOLD 1     /* running min/max <- key of the previous token */
 #define QQ_STEP_FINALIZE 2 /* finalize pages whose 64th token arrived, advance counters */

@@ -78,6 +78,29 @@ class QQNewToken(ctypes.Structure):
     ]
 
 
+class QQExtendBatch(ctypes.Structure):
+    _fields_ = [
+        ("req_pool_indices", c_void_p),
+        ("seq_lens", c_void_p),
+        ("prefix_lens", c_void_p),
+        ("token_offsets", c_void_p),
+        ("out_cache_loc", c_void_p),
+        ("num_tokens", c_int64),
+        ("bs", c_int32),
+        ("max_seq_len", c_int32),
+    ]
+
+
+class QQHotBuffer(ctypes.Structure):
+    _fields_ = [
+        ("k", c_void_p),
+        ("v", c_void_p),
+        ("row_stride", c_int64),
+        ("device_buffer_size", c_int64),
+        ("num_rows", c_int64),
+    ]
+
+
 class QQHiSparseState(ctypes.Structure):
     _fields_ = [
         ("buffer_tokens", c_void_p),
@@ -97,6 +120,8 @@ _B = POINTER(QQBatch)
 _T = POINTER(QQTokenTable)
 _N = POINTER(QQNewToken)
 _H = POINTER(QQHiSparseState)
+_E = POINTER(QQExtendBatch)
+_HB = POINTER(QQHotBuffer)
 _PP = POINTER(c_void_p)
 
 #: every exported symbol with its (restype, argtypes); tests check the list
@@ -110,6 +135,9 @@ SIGNATURES: dict[str, tuple] = {
     "qq_quest_invalidate": (c_int, [_S, c_int, c_void_p]),
     "qq_quest_bounds_prefill": (
         c_int, [_S, c_int, c_int, _PP, c_int, c_int64, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "qq_quest_extend_kv": (
+        c_int, [_S, c_int, c_int, _E, _T, c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p,
+                c_int64, c_int64, _HB, c_void_p, c_void_p]),
     "qq_quest_decode_step": (
         c_int, [_S, c_int, c_int, c_int, _PP, c_int, c_int64, _B, c_void_p, c_void_p, _T, c_int64,
                 c_void_p, c_size_t, c_void_p]),
@@ -198,7 +226,9 @@ def ptr_array(ptrs: list[int]):
 __all__ = [
     "QQBatch",
     "QQError",
+    "QQExtendBatch",
     "QQHiSparseState",
+    "QQHotBuffer",
     "QQNewToken",
     "QQQuestState",
     "QQTokenTable",

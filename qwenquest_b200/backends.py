@@ -17,12 +17,18 @@ the current stream with no host synchronisation:
   Mode 3 one ``qq_hisparse_swap_in`` launch, and one
   ``qq_sparse_decode_attention`` launch.
 
-Prefill stays dense, as in the reference (``attention/base.py:65-93``).
+Prefill attention stays dense, as in the reference (``attention/base.py:65-93``);
+per prefill layer one ``qq_quest_extend_kv`` launch writes the new K/V rows
+and builds that layer's Quest bounds from them (Mode 3 also fills the hot
+buffer and backs the layer up to the host tier on a side stream), where the
+reference writes the pool and re-reads every key for the bounds after the
+last layer.
 """
 
 from __future__ import annotations
 
 from abc import ABC, abstractmethod
+from dataclasses import dataclass
 
 import torch
 import torch.nn.functional as F
@@ -81,6 +87,10 @@ class AttentionBackend(ABC):
         assert batch.out_cache_loc is not None
         assert batch.extend_prefix_lens is not None
         self.token_to_kv_pool.set_kv_buffer(layer.layer_id, batch.out_cache_loc, k, v)
+        return self._extend_attention(q, layer, batch)
+
+    def _extend_attention(self, q, layer, batch) -> torch.Tensor:
+        """The attention half of ``forward_extend``, over the K/V rows already in the pool."""
         k_buf, v_buf = self.token_to_kv_pool.get_kv_buffer(layer.layer_id)
         offsets = batch.extend_token_offsets()
         outputs = []
@@ -112,6 +122,19 @@ def _parse_quest_config(sparse_config):
     return cfg
 
 
+@dataclass
+class _ExtendPlan:
+    """The per-batch constants of every prefill layer's ``qq_quest_extend_kv`` launch."""
+
+    batch: object
+    reqs: list[int]
+    seq_lens: list[int]
+    tensors: tuple  # device int64 tensors the struct points into
+    qq: _lib.QQExtendBatch
+    unfused: bool = False
+    admission: object = None
+
+
 class _QuestDecodeMixin:
     """Shared decode plumbing: step tensors, persistent buffers, the attention launch."""
 
@@ -140,6 +163,12 @@ class _QuestDecodeMixin:
         #: selection and attention in one call (qq_quest_decode_attention) when
         #: nothing traces the selection or times the kernels one by one
         self.fused = True
+        #: prefill K/V write, bounds (and Mode 3 hot buffer) in one launch per
+        #: layer (qq_quest_extend_kv); False keeps the reference's order:
+        #: set_kv_buffer per layer, bounds from the pool after the last layer
+        self.fused_extend = True
+        self._xplan: _ExtendPlan | None = None
+        self._xerr = _DeviceError(torch.zeros(1, dtype=torch.int32).pin_memory())
 
     def _ev_begin(self):
         if self.kernel_events is None:
@@ -176,6 +205,65 @@ class _QuestDecodeMixin:
     def check_errors(self) -> None:
         """Raise for device errors reported by earlier launches (no synchronisation)."""
         _lib.raise_device_error(self._attn_err.take(), "(attention)")
+        _lib.raise_device_error(self._xerr.take(), "(prefill K/V write)")
+
+    # ----------------------------------------------------------------- prefill
+
+    def _extend_plan(self, batch) -> _ExtendPlan:
+        """Device copies of the batch's request, length, prefix and offset arrays (once per batch)."""
+        plan = self._xplan
+        if plan is not None and plan.batch is batch:
+            return plan
+        dev = self.device
+        reqs = batch.req_pool_indices.to(device=dev, dtype=torch.int64).contiguous()
+        seq = batch.seq_lens.to(device=dev, dtype=torch.int64).contiguous()
+        if batch.extend_prefix_lens is None:
+            prefix = torch.zeros_like(seq)
+        else:
+            prefix = batch.extend_prefix_lens.to(device=dev, dtype=torch.int64).contiguous()
+        seq_h = [int(x) for x in seq.tolist()]
+        if batch.extend_seq_lens is None:
+            new_h = [n - p for n, p in zip(seq_h, prefix.tolist(), strict=True)]
+        else:
+            new_h = [int(x) for x in batch.extend_seq_lens.tolist()]
+        if any(n < 0 for n in new_h) or any(
+                s - p != n for s, p, n in zip(seq_h, prefix.tolist(), new_h, strict=True)):
+            raise ValueError("extend batch: seq_lens must equal extend_prefix_lens + extend_seq_lens")
+        offsets_h = [0]
+        for n in new_h[:-1]:
+            offsets_h.append(offsets_h[-1] + n)
+        offsets = torch.tensor(offsets_h, dtype=torch.int64, device=dev)
+        loc = batch.out_cache_loc.to(device=dev, dtype=torch.int64).contiguous()
+        if loc.numel() != sum(new_h):
+            raise ValueError(f"extend batch: {loc.numel()} out_cache_loc rows for {sum(new_h)} new tokens")
+        qq = _lib.QQExtendBatch(reqs.data_ptr(), seq.data_ptr(), prefix.data_ptr(), offsets.data_ptr(),
+                                loc.data_ptr(), loc.numel(), len(seq_h), max(seq_h, default=0))
+        plan = _ExtendPlan(batch, [int(x) for x in reqs.tolist()], seq_h, (reqs, seq, prefix, offsets, loc), qq)
+        self._xplan = plan
+        return plan
+
+    def _extend_write(self, k, v, layer_id: int, plan: _ExtendPlan, hot=None) -> None:
+        """[Q2] one prefill layer: new K/V rows into the pool and this layer's bounds, one launch."""
+        k_buf, v_buf = self.token_to_kv_pool.get_kv_buffer(layer_id)
+        q = self.quest
+        dim = q.kv_heads * q.head_dim
+        n = k.shape[0]
+        kk = k.to(k_buf.dtype).reshape(n, dim)
+        vv = v.to(v_buf.dtype).reshape(n, dim)
+        if kk.stride(1) != 1 or vv.stride(1) != 1 or kk.stride(0) != vv.stride(0):
+            kk, vv = kk.contiguous(), vv.contiguous()
+        in_quest = q.start_layer <= layer_id < q.end_layer
+        rc = self.lib.qq_quest_extend_kv(
+            q._state if in_quest else None, layer_id - q.start_layer, int(layer_id == q.end_layer - 1),
+            plan.qq, self._token_table(), kk.data_ptr(), vv.data_ptr(), dtype_code(k_buf.dtype), dim,
+            kk.stride(0), k_buf.data_ptr(), v_buf.data_ptr(), k_buf.stride(0), k_buf.shape[0], hot,
+            self._xerr.ptr(), stream_of(self.device),
+        )
+        check(rc, "prefill K/V write")
+
+    def _extend_fusable(self) -> bool:
+        pool = self.token_to_kv_pool
+        return self.fused_extend and pool.dtype in (torch.bfloat16, torch.float32)
 
     def synchronize(self) -> None:
         """Wait for this backend's work and raise any device error it reported."""
@@ -270,8 +358,19 @@ class B200QuestOnlyBackend(_QuestDecodeMixin, AttentionBackend):
     # ----------------------------------------------------------------- prefill
 
     def forward_extend(self, q, k, v, layer, batch) -> torch.Tensor:
+        li = layer.layer_id
+        plan = self._extend_plan(batch)
+        if self._extend_fusable() and not plan.unfused:
+            # [Q2] K/V write + this layer's bounds in one launch
+            assert batch.out_cache_loc is not None
+            self._extend_write(k, v, li, plan)
+            out = self._extend_attention(q, layer, batch)
+            if li == self.quest.end_layer - 1:
+                self._skip_first_decode_update.index_fill_(0, plan.tensors[0], 1)
+            return out
+        plan.unfused = True
         out = super().forward_extend(q, k, v, layer, batch)
-        if layer.layer_id == self.quest.end_layer - 1:
+        if li == self.quest.end_layer - 1:
             self._update_quest_for_extend(batch)
         return out
 
@@ -381,7 +480,29 @@ class B200QuestHiSparseBackend(_QuestDecodeMixin, AttentionBackend):
             self.coord.prepare_decode_step(batch.req_pool_indices, batch.seq_lens)
             self._begin_step(batch)
 
+    def forward_extend(self, q, k, v, layer, batch) -> torch.Tensor:
+        li = layer.layer_id
+        plan = self._extend_plan(batch)
+        if self._extend_fusable() and not plan.unfused:
+            # [H1] + [Q2] K/V write, hot buffer and this layer's bounds in one
+            # launch; the layer's host backup follows on a side stream
+            assert batch.out_cache_loc is not None
+            if plan.admission is None:
+                plan.admission = self.coord.begin_admission(plan.reqs, plan.seq_lens, self.req_to_token)
+            self._extend_write(k, v, li, plan, hot=self.coord.hot_buffer(li))
+            self.coord.backup_layer(plan.admission, li, self.token_to_kv_pool)
+            return self._extend_attention(q, layer, batch)
+        if plan.admission is not None:
+            raise RuntimeError("a prefill batch switched from the fused K/V write to set_kv_buffer")
+        plan.unfused = True
+        return super().forward_extend(q, k, v, layer, batch)
+
     def on_extend_finished(self, batch) -> None:
+        plan = self._xplan
+        if plan is not None and plan.batch is batch and plan.admission is not None:
+            self.coord.finish_admission(plan.admission)
+            self._xplan = None
+            return
         for req_idx, seq_len in zip(batch.req_pool_indices.tolist(), batch.seq_lens.tolist(), strict=True):
             prefill_indices = self.req_to_token[req_idx, :seq_len]
             self.coord.admit_request(req_idx, seq_len, self.token_to_kv_pool, prefill_indices)

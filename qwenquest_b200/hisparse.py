@@ -86,6 +86,16 @@ class _DeviceError:
         return bits
 
 
+@dataclass
+class _Admission:
+    """A prefill batch being admitted layer by layer."""
+
+    reqs: list[int]
+    src_rows: torch.Tensor  # device int32: pool row of every prefill position, requests in order
+    host_rows: torch.Tensor  # device int64: the host-tier row it is backed up to
+    layers: int = 0
+
+
 class HiSparseCoordinator:
     def __init__(
         self,
@@ -147,6 +157,7 @@ class HiSparseCoordinator:
         self._lru_init = torch.arange(buf, dtype=torch.int32, device=dev)
         self.lru_slots = self._lru_init.repeat(num_layers, max_reqs, 1).contiguous()
         self._skip_first_backup = [False] * max_reqs
+        self._backup_stream: torch.cuda.Stream | None = None
         self._stats = torch.zeros(3, dtype=torch.int64, device=dev)
         self.stats = SwapInStats(self._stats)
         self._err = _DeviceError(torch.zeros(1, dtype=torch.int32).pin_memory())
@@ -157,7 +168,8 @@ class HiSparseCoordinator:
         self.row_bytes = kv_heads * head_dim * torch.empty(0, dtype=dtype).element_size()
         # per-layer pointer arrays (K layers then V layers)
         self._dev_ptrs = _lib.ptr_array([t.data_ptr() for t in self.device_k + self.device_v])
-        self._host_ptrs = _lib.ptr_array([host_device_pointer(t) for t in self.host_k + self.host_v])
+        self._host_dev = [host_device_pointer(t) for t in self.host_k + self.host_v]
+        self._host_ptrs = _lib.ptr_array(self._host_dev)
         self._dev_k_ptrs = _lib.ptr_array([t.data_ptr() for t in self.device_k[quest.start_layer:quest.end_layer]])
 
     def _stream(self) -> int:
@@ -196,6 +208,56 @@ class HiSparseCoordinator:
         q.update_prefill_representations_all_layers(req, kb[q.start_layer:q.end_layer], idx)
         self._skip_first_backup[req] = True
         del keep
+
+    # ------------------------------------ [H1] admission fused with the prefill
+
+    def begin_admission(self, reqs: list[int], seq_lens: list[int], req_to_token: torch.Tensor) -> _Admission:
+        """Host rows for a prefill batch, taken before its first layer so each layer backs up as it goes.
+
+        The layers' K/V writes (``qq_quest_extend_kv`` with this coordinator's
+        hot buffer) fill the device tier and the bounds; :meth:`backup_layer`
+        copies each layer's rows to the host tier on a side stream, overlapped
+        with the following layers; :meth:`finish_admission` joins it and lays
+        out the slots.  Together the same state as :meth:`admit_request`
+        (``coordinator.py:138-174``).
+        """
+        src, dst = [], []
+        for req, n in zip(reqs, seq_lens, strict=True):
+            host_idx_dev = self.host_allocator.alloc(n).to(self.device)
+            self.req_to_host_pool[req, :n] = host_idx_dev.to(torch.int32)
+            src.append(req_to_token[req, :n].to(torch.int32))
+            dst.append(host_idx_dev.to(torch.int64))
+        if self._backup_stream is None:
+            self._backup_stream = torch.cuda.Stream(device=self.device)
+        return _Admission(list(reqs), torch.cat(src).contiguous(), torch.cat(dst).contiguous())
+
+    def hot_buffer(self, layer_id: int) -> _lib.QQHotBuffer:
+        kd, vd = self.device_k[layer_id], self.device_v[layer_id]
+        return _lib.QQHotBuffer(kd.data_ptr(), vd.data_ptr(), kd.stride(0), self.device_buffer_size, kd.shape[0])
+
+    def backup_layer(self, adm: _Admission, layer_id: int, token_to_kv_pool) -> None:
+        """Copy layer ``layer_id``'s prefill rows to the host tier, behind that layer's K/V write."""
+        kb, vb = token_to_kv_pool.get_kv_buffer(layer_id)
+        side = self._backup_stream
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        src, keep_s = _lib.ptr_array([kb.data_ptr(), vb.data_ptr()])
+        dst, keep_d = _lib.ptr_array([self._host_dev[layer_id], self._host_dev[self.num_layers + layer_id]])
+        check(self.lib.qq_copy_rows(src, dst, 2, kb.stride(0) * kb.element_size(), self.row_bytes,
+                                    self.row_bytes, adm.src_rows.data_ptr(), 0, adm.host_rows.data_ptr(), 1,
+                                    adm.host_rows.numel(), side.cuda_stream),
+              "admission host backup")
+        del keep_s, keep_d
+        adm.layers += 1
+
+    def finish_admission(self, adm: _Admission) -> None:
+        """Join the host backups and set each request's slot layout (the end of ``admit_request``)."""
+        if adm.layers != self.num_layers:
+            raise RuntimeError(f"admission backed up {adm.layers} of {self.num_layers} layers")
+        torch.cuda.current_stream(self.device).wait_stream(self._backup_stream)
+        s = self._stream()
+        for req in adm.reqs:
+            check(self.lib.qq_hisparse_admit_layout(self._hs, req, s), "admit_request layout")
+            self._skip_first_backup[req] = True
 
     # -------------------------------------------------- [H2] per decode step
 
