@@ -9,8 +9,8 @@
 // through req_to_token.
 //
 // Block (page, request, row chunk), 256 threads: the threads of a row group
-// cover 16 of a row's 16-byte words (4-byte words when the rows or pointers
-// are not 16-byte aligned) and the 16 row groups walk the page's positions; each
+// cover 16-64 of a row's 16-byte words (4-byte words when the rows or pointers
+// are not 16-byte aligned) and the 4-16 row groups walk the page's positions; each
 // thread keeps the min / max of its channels (bf16 pairs packed, fp32 as
 // is), the row groups are folded in shared memory and fp32 is rounded to bf16
 // once (rounding is monotone).  Loads
@@ -25,10 +25,25 @@ namespace {
 
 constexpr int kExtendThreads = 256;
 constexpr int kExtendUnroll = 4;
-// Words of a row one block covers: 16 x 16 bytes, so a 1 KiB row spreads over
-// 4 blocks and a 32K-token layer makes 2048 blocks; the block scheduler then
-// balances the tail (with whole rows per block, 512 blocks made 1.15 waves).
-constexpr int kExtendWordsPerBlock = 16;
+// Words of a row one block covers: at most 64 (a whole 1 KiB bf16 row), halved
+// (down to 16) while the launch would give fewer than 4 blocks per SM — 4 is
+// the residency at this kernel's register count.  Measured on a 32K-token
+// layer: 64 or 32 words per block 1.376 / 1.379 ms per 48 layers, 16 words
+// 1.475, 8 words 1.77 (more, smaller blocks add per-block latency).
+constexpr int kExtendMaxWordsPerBlock = 64;
+constexpr int kExtendMinWordsPerBlock = 16;
+constexpr int kExtendBlocksPerSm = 4;
+
+int extend_sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
 
 struct ExtendArgs {
   qq_quest_state st;
@@ -115,7 +130,7 @@ __device__ __forceinline__ uint16_t channel_bits(const uint32_t (&w)[NW], int e)
 }
 
 template <typename T, int VB>
-__global__ void __launch_bounds__(kExtendThreads, 4) extend_kv_kernel(ExtendArgs a) {
+__global__ void __launch_bounds__(kExtendThreads, kExtendBlocksPerSm) extend_kv_kernel(ExtendArgs a) {
   using Vec = typename VecOf<VB>::type;
   constexpr int NW = VB / 4;                        // 32-bit words per vector word
   constexpr int CH = VB / (int)sizeof(T);           // channels per vector word
@@ -362,10 +377,15 @@ extern "C" int qq_quest_extend_kv(const qq_quest_state* st, int layer, int write
     a.hot_rows = hot->num_rows;
   }
   a.words = (int)(row_bytes / vb);
-  a.wpb = a.words < kExtendWordsPerBlock ? a.words : kExtendWordsPerBlock;
+  const unsigned pages = (unsigned)((eb->max_seq_len + page_size - 1) / page_size);
+  int wpb = a.words < kExtendMaxWordsPerBlock ? a.words : kExtendMaxWordsPerBlock;
+  const int64_t want = (int64_t)extend_sm_count() * kExtendBlocksPerSm;
+  while (wpb > kExtendMinWordsPerBlock && wpb % 2 == 0 &&
+         (int64_t)pages * eb->bs * ((a.words + wpb - 1) / wpb) < want)
+    wpb /= 2;
+  a.wpb = wpb;
   a.row_groups = kExtendThreads / a.wpb;
   a.err = err;
-  const unsigned pages = (unsigned)((eb->max_seq_len + page_size - 1) / page_size);
   const unsigned chunks = (unsigned)((a.words + a.wpb - 1) / a.wpb);
   dim3 grid(pages, (unsigned)eb->bs, chunks);
   cudaStream_t s = as_stream(stream);

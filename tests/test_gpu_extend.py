@@ -183,3 +183,17 @@ def test_hisparse_admission_fused_equals_reference_order(dtype, kv, d, cuda_devi
             assert torch.equal(ca.host_v[li][host], pool.v_buffer[li][rows].cpu())
             assert torch.equal(ca.device_k[li][r * (BUF + 1): r * (BUF + 1) + hot], pool.k_buffer[li][rows[:hot]])
             assert torch.equal(ca.device_v[li][r * (BUF + 1): r * (BUF + 1) + hot], pool.v_buffer[li][rows[:hot]])
+
+
+def test_quest_extend_large_batch(cuda_device):
+    """Enough pages that a launch covers half rows (32 words) per block instead of quarter rows."""
+    runs = [_Run("quest", torch.bfloat16, 4, 128, fused, cuda_device, seed=3) for fused in (True, False)]
+    reqs, new = list(range(MAX_REQS)), [1000, 999, 1001 - 64, 640, 1017, 1008, 961, 1023]
+    outs = [r.extend(reqs, [0] * MAX_REQS, new) for r in runs]
+    for oa, ob in zip(*outs, strict=True):
+        assert torch.equal(oa, ob)
+    torch.cuda.synchronize(cuda_device)
+    for r in runs:
+        r.be.check_errors()
+    _assert_same_state(*runs)
+    _assert_oracle_bounds(runs[0], reqs, new)
