@@ -325,6 +325,253 @@ def prefill_case(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- configs 2 and 3
+
+
+def _decode_inputs(dev, gen, steps, n_layers, n_req, q_ar=0.0):
+    """Per-step decode inputs ``[steps, layers, n_req, ...]`` (bf16): q (AR(1) over steps when q_ar), new K/V."""
+    q = torch.empty((steps, n_layers, n_req, H, D), dtype=torch.bfloat16, device=dev)
+    state = torch.randn((n_layers, n_req, H, D), generator=gen, device=dev)
+    for s in range(steps):
+        if s:
+            state = q_ar * state + torch.randn(state.shape, generator=gen, device=dev) if q_ar else \
+                torch.randn(state.shape, generator=gen, device=dev)
+        q[s].copy_(state)
+    k = torch.randn((steps, n_layers, n_req, KV, D), generator=gen, device=dev).to(torch.bfloat16)
+    v = torch.randn((steps, n_layers, n_req, KV, D), generator=gen, device=dev).to(torch.bfloat16)
+    return q, k, v
+
+
+def _kernel_ms(backend, batches, layers, inputs, first, last) -> dict:
+    """Mean CUDA-event duration per kernel over steps [first, last) (the backend's per-launch events)."""
+    backend.kernel_events = {}
+    _timed_steps(backend, batches, layers, inputs, first, last)
+    kev, backend.kernel_events = backend.kernel_events, None
+    return {k: statistics.mean(a.elapsed_time(b) for a, b in v) for k, v in kev.items()}
+
+
+def _timed_steps(backend, batches, layers, inputs, first, last):
+    qs, ks, vs = inputs
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for s in range(first, last):
+        run_step(backend, batches[s], layers, (qs[s], ks[s], vs[s]))
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b)
+
+
+def config2_case(args) -> None:
+    """``--case config2``: 16 ragged requests (14 at 65,537-131,073 tokens, 2 dense), 48 layers, Mode 2.
+
+    K = s * (W + N(0,1)) with W a per-(head, channel) random walk along the
+    positions (step N(0, 0.02^2)) and s ~ LogNormal(0, 0.5) per channel;
+    V = s * N(0,1).  ``RESIDENT`` physical KV buffers alias the 48 layers as
+    in config 1.  Steps go through the drop-in backend exactly as config 1.
+    """
+    from types import SimpleNamespace
+
+    from qwenquest_b200.backends import B200QuestOnlyBackend
+    from qwenquest_b200.batch import ForwardBatch, ForwardMode
+    from qwenquest_b200.memory import ReqToTokenPool
+    from qwenquest_b200.workloads import torch_generator
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rng = np.random.default_rng(args.seed + 2)
+    prefixes = [int(x) for x in rng.integers(65536, 131073, size=14)]
+    prefixes = [x + 1 if x % PAGE == 0 else x for x in prefixes] + [int(x) for x in rng.integers(1, 2048, size=2)]
+    n_req, n_layers, resident = len(prefixes), args.layers, min(args.resident, args.layers)
+    warm = args.warmup
+    total = warm + args.steps
+    kstep = min(5, args.steps)  # steps of the per-kernel timing pass, after the timed ones
+    total += kstep
+    max_ctx = ((max(prefixes) + total + 1 + PAGE - 1) // PAGE) * PAGE
+    rows = n_req * max_ctx + 1
+    gen = torch_generator(dev, args.seed + 2)
+    k_phys, v_phys = [], []
+    for _ in range(resident):
+        k_phys.append(torch.zeros((rows, KV, D), dtype=torch.bfloat16, device=dev))
+        v_phys.append(torch.zeros((rows, KV, D), dtype=torch.bfloat16, device=dev))
+    pool = _Pool(k_phys, v_phys, n_layers)
+    r2t = ReqToTokenPool(n_req, max_ctx, dev)
+    r2t.req_to_token.copy_(
+        (1 + torch.arange(n_req, device=dev)[:, None] * max_ctx + torch.arange(max_ctx, device=dev)[None])
+        .to(torch.int32))
+    backend = B200QuestOnlyBackend(r2t, pool, {"algorithm": "quest", "top_k": TOP_K, "quest_page_size": PAGE})
+    q = backend.quest
+    for r in range(resident):
+        scale = torch.exp(0.5 * torch.randn(KV, D, generator=gen, device=dev))
+        for i, n in enumerate(prefixes):
+            walk = torch.randn((n, KV, D), generator=gen, device=dev).mul_(0.02).cumsum_(0)
+            k = walk.add_(torch.randn((n, KV, D), generator=gen, device=dev)).mul_(scale)
+            base = 1 + i * max_ctx
+            k_phys[r][base:base + n].copy_(k)
+            v_phys[r][base:base + n].copy_(torch.randn((n, KV, D), generator=gen, device=dev).mul_(scale))
+            del walk, k
+            q.update_prefill_representations(r, i, k_phys[r], r2t.req_to_token[i, :n])
+    for layer in range(resident, n_layers):
+        q.page_k_bounds[layer].copy_(q.page_k_bounds[layer % resident])
+        q.running_k_min[layer].copy_(q.running_k_min[layer % resident])
+        q.running_k_max[layer].copy_(q.running_k_max[layer % resident])
+    pre = torch.tensor(prefixes, dtype=torch.int64, device=dev)
+    q.running_token_count.copy_((pre % PAGE).to(torch.int32))
+    q.running_page_idx.copy_((pre // PAGE).to(torch.int32))
+    backend._skip_first_decode_update.fill_(1)
+    inputs = _decode_inputs(dev, gen, total, n_layers, n_req)
+    reqs = torch.arange(n_req, dtype=torch.int64, device=dev)
+    batches = []
+    for s in range(total):
+        pos = pre + s
+        batches.append(ForwardBatch(
+            forward_mode=ForwardMode.DECODE, input_ids=torch.zeros(n_req, dtype=torch.int64, device=dev),
+            positions=pos, req_pool_indices=reqs, seq_lens=pos + 1, out_cache_loc=1 + reqs * max_ctx + pos,
+            req_to_token_pool=r2t, token_to_kv_pool=pool, attn_backend=backend))
+    layers = [SimpleNamespace(layer_id=i, scaling=D ** -0.5, num_heads=H, num_kv_heads=KV, head_dim=D)
+              for i in range(n_layers)]
+    torch.cuda.synchronize(dev)
+    _timed_steps(backend, batches, layers, inputs, 0, warm)
+    clocks = ClockSampler(0)
+    clocks.start()
+    ms = _timed_steps(backend, batches, layers, inputs, warm, warm + args.steps)
+    clock_info = clocks.stop()
+    kernel_ms = _kernel_ms(backend, batches, layers, inputs, warm + args.steps, total)
+    backend.check_errors()
+    # algorithmic bytes per layer-step at the timed steps' mean length
+    step_bytes = 0
+    for n in prefixes:
+        L = n + 1 + warm + args.steps // 2
+        step_bytes += 4_233_216 + 2048 * (L // PAGE) if L > TOP_K else 30_720 + 2052 * L
+    value = n_layers * args.steps / (ms / 1e3)
+    peak, peak_kind = measured_peaks()
+    gbs = step_bytes * value / 1e9
+    print(json.dumps({
+        "case": "config2", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": warm, "ms_per_step": ms / args.steps, "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic (K = s*(random walk, step N(0,0.02^2), + N(0,1)), V = s*N(0,1), q N(0,1))",
+        "config": {"workload": "config2: 16 requests (14 long at 65,537-131,073 tokens ending in a partial page, "
+                               "2 dense-fallback), 48 layers, Quest top_k 2048 / page 64, quest mode",
+                   "prefixes": prefixes, "resident_kv_layers": resident,
+                   "l2": "inputs larger than L2 (~109 MB of distinct data per layer-step)"},
+        "layer_step_bytes": step_bytes, "layer_step_gbs": gbs,
+        "kernel_ms": kernel_ms,
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "peak_kind": peak_kind, "scope": "whole layer step"},
+        "clocks": clock_info,
+    }), flush=True)
+
+
+def config3_case(args) -> None:
+    """``--case config3``: Mode 3 (HiSparse), 32 requests at 65,536 tokens, 48 layers.
+
+    The full KV lives in the pinned host tier (``host_layers=1``: the 48
+    layers share one host buffer, as the full 48-layer history would need
+    ~200 GB of host RAM; the bytes moved are the same), each request keeps a
+    4096 + 1 slot hot buffer per layer, and decode queries follow
+    q[t+1] = 0.9 q[t] + N(0,1), so each step misses part of its selection.
+    Prefill is admitted through ``on_extend_finished`` (host backup, hot
+    buffer, bounds).  Reported: layer-steps/s after warm-up, the hit rate and
+    the swap-in bytes of the timed steps, against the host-link roofline
+    (pinned host -> device copy bandwidth measured in the same run).
+    """
+    from types import SimpleNamespace
+
+    from qwenquest_b200.backends import B200QuestHiSparseBackend
+    from qwenquest_b200.batch import ForwardBatch, ForwardMode
+    from qwenquest_b200.memory import MHATokenToKVPool, ReqToTokenPool
+    from qwenquest_b200.workloads import fill_rows_normal_, torch_generator
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_req, prefix, n_layers, buf = 32, 65536, args.layers, 4096
+    warm = max(args.warmup, 8)
+    kstep = min(5, args.steps)
+    total = warm + args.steps + kstep
+    # (one extra page: the eager backup takes one host row per request and step)
+    max_ctx = ((prefix + total + 1 + PAGE - 1) // PAGE) * PAGE + PAGE
+    gen = torch_generator(dev, args.seed + 3)
+    r2t = ReqToTokenPool(n_req, max_ctx, dev)
+    pool = MHATokenToKVPool(prefix, n_layers, KV, D, torch.bfloat16, dev)
+    backend = B200QuestHiSparseBackend(
+        r2t, pool, {"algorithm": "quest", "top_k": TOP_K, "quest_page_size": PAGE, "device_buffer_size": buf},
+        host_pool_size=n_req * max_ctx, host_layers=1)
+    scale = torch.exp(0.5 * torch.randn(KV, D, generator=gen, device=dev))
+    locs = torch.arange(1, prefix + 1, dtype=torch.int64, device=dev)
+    for _ in range(n_req):
+        slot = r2t.alloc()
+        r2t.req_to_token[slot, :prefix] = locs.to(torch.int32)
+        for li in range(n_layers):
+            fill_rows_normal_(pool.k_buffer[li][1:], scale, gen)
+            fill_rows_normal_(pool.v_buffer[li][1:], scale, gen)
+        one = torch.ones(1, dtype=torch.int64, device=dev)
+        backend.on_extend_finished(ForwardBatch(
+            forward_mode=ForwardMode.EXTEND, input_ids=torch.zeros(prefix, dtype=torch.int64, device=dev),
+            positions=locs - 1, req_pool_indices=one * slot, seq_lens=one * prefix, out_cache_loc=locs,
+            req_to_token_pool=r2t, token_to_kv_pool=pool, attn_backend=backend,
+            extend_prefix_lens=one * 0, extend_seq_lens=one * prefix))
+        r2t.req_to_token[slot, :prefix] = 0  # the engine frees the prefill rows after admission
+    torch.cuda.synchronize(dev)
+    inputs = _decode_inputs(dev, gen, total, n_layers, n_req, q_ar=0.9)
+    reqs = torch.arange(n_req, dtype=torch.int64, device=dev)
+    batches = []
+    for s in range(total):
+        pos = torch.full((n_req,), prefix + s, dtype=torch.int64, device=dev)
+        batches.append(ForwardBatch(
+            forward_mode=ForwardMode.DECODE, input_ids=torch.zeros(n_req, dtype=torch.int64, device=dev),
+            positions=pos, req_pool_indices=reqs, seq_lens=pos + 1, out_cache_loc=None,
+            req_to_token_pool=r2t, token_to_kv_pool=pool, attn_backend=backend))
+    layers = [SimpleNamespace(layer_id=i, scaling=D ** -0.5, num_heads=H, num_kv_heads=KV, head_dim=D)
+              for i in range(n_layers)]
+    stats = backend.coord.stats
+    _timed_steps(backend, batches, layers, inputs, 0, warm)
+    h0, m0 = stats.hits, stats.misses
+    clocks = ClockSampler(0)
+    clocks.start()
+    ms = _timed_steps(backend, batches, layers, inputs, warm, warm + args.steps)
+    clock_info = clocks.stop()
+    backend.check_errors()
+    hits, misses = stats.hits - h0, stats.misses - m0
+    kernel_ms = _kernel_ms(backend, batches, layers, inputs, warm + args.steps, total)
+    # the host link: a 1 GiB pinned host -> device copy, best of 3
+    host = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    devbuf = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    best = float("inf")
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        devbuf.copy_(host, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize(dev)
+        best = min(best, a.elapsed_time(b))
+    link_gbs = (1 << 30) / (best / 1e3) / 1e9
+    del host, devbuf
+    layer_steps = n_layers * args.steps
+    value = layer_steps / (ms / 1e3)
+    row2 = 2 * KV * D * 2  # K and V row of one position
+    swap_bytes = misses * row2 / layer_steps  # per layer-step
+    L = prefix + 1 + warm + args.steps // 2
+    hbm_bytes = n_req * (4_233_216 + 2048 * (L // PAGE) + 4 * buf * 4) + swap_bytes
+    peak, peak_kind = measured_peaks()
+    t_hbm = hbm_bytes / (peak * 1e9)
+    t_link = swap_bytes / (link_gbs * 1e9)
+    t_roof = max(t_hbm, t_link)
+    print(json.dumps({
+        "case": "config3", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": warm, "ms_per_step": ms / args.steps, "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic (K, V = s*N(0,1); q AR(1), rho 0.9)",
+        "config": {"workload": "config3: 32 requests x 65,536 tokens, 48 layers, HiSparse (pinned host tier, "
+                               "4096+1 slot hot buffer), Quest top_k 2048 / page 64", "host_layers": 1},
+        "hit_rate": hits / max(1, hits + misses), "misses_per_layer_step": misses / layer_steps,
+        "swap_in_bytes_per_layer_step": swap_bytes, "hbm_bytes_per_layer_step": hbm_bytes,
+        "kernel_ms": kernel_ms,
+        "host_link": {"achieved_gbs": swap_bytes * value / 1e9, "pinned_h2d_copy_gbs": link_gbs},
+        "roofline": {"bound": "host link" if t_link >= t_hbm else "hbm",
+                     "roofline_layer_steps_per_s": 1.0 / t_roof, "frac": value * t_roof,
+                     "hbm_peak_gbs": peak, "peak_kind": peak_kind},
+        "clocks": clock_info,
+    }), flush=True)
+
+
 # --------------------------------------------------------------------------- CPU baseline
 
 
@@ -445,15 +692,16 @@ def main() -> None:
     ap.add_argument("--requests", type=int, default=N_REQ, help="requests per GPU (profiling cases only)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers (profiling cases only)")
     ap.add_argument("--resident", type=int, default=RESIDENT, help="physical KV buffers")
-    ap.add_argument("--case", choices=["decode", "prefill"], default="decode",
-                    help="decode: the benchmark (default); prefill: the prefill K/V write + bounds (1 GPU)")
+    ap.add_argument("--case", choices=["decode", "prefill", "config2", "config3"], default="decode",
+                    help="decode: the benchmark, config 1 (default); prefill: the prefill K/V write + bounds; "
+                         "config2 / config3: the ragged and HiSparse benchmark configs (1 GPU each)")
     ap.add_argument("--strong", action="store_true",
                     help="shard --requests over the GPUs (strong scaling) instead of --requests per GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.case == "prefill":
+    if args.case != "decode":
         if int(os.environ.get("RANK", "0")) == 0:
-            prefill_case(args)
+            {"prefill": prefill_case, "config2": config2_case, "config3": config3_case}[args.case](args)
         return
     from qwenquest_b200.sharding import max_over_ranks, shard_requests
 
