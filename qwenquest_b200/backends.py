@@ -374,6 +374,10 @@ class B200QuestOnlyBackend(_QuestDecodeMixin, AttentionBackend):
             self._update_quest_for_extend(batch)
         return out
 
+    def on_extend_finished(self, batch) -> None:
+        if self._xplan is not None and self._xplan.batch is batch:
+            self._xplan = None  # the prefill's device index arrays
+
     def _update_quest_for_extend(self, batch) -> None:
         """[Q2] bounds of positions ``0 .. seq_len-1`` of every layer (quest_only.py:101-128)."""
         q = self.quest
