@@ -152,13 +152,15 @@ class _Pool:
 
 
 def build_config1(dev, total_steps: int, seed: int, n_req: int = N_REQ, prefix: int = PREFIX,
-                  layers: int = LAYERS, resident: int = RESIDENT):
+                  layers: int = LAYERS, resident: int = RESIDENT, context_limit: int | None = None):
     from qwenquest_b200.backends import B200QuestOnlyBackend
     from qwenquest_b200.memory import ReqToTokenPool
     from qwenquest_b200.workloads import fill_rows_normal_, torch_generator
 
     max_ctx = ((prefix + total_steps + 1 + PAGE - 1) // PAGE) * PAGE
     rows = n_req * max_ctx + 1
+    # the engine's max_context_len (req_to_token and Quest storage); pool rows stay max_ctx per request
+    limit = max_ctx if context_limit is None else max(max_ctx, context_limit)
     gen = torch_generator(dev, seed)
     k_phys, v_phys = [], []
     for r in range(resident):
@@ -170,9 +172,9 @@ def build_config1(dev, total_steps: int, seed: int, n_req: int = N_REQ, prefix: 
         k_phys.append(kb)
         v_phys.append(vb)
     pool = _Pool(k_phys, v_phys, layers)
-    r2t = ReqToTokenPool(n_req, max_ctx, dev)
+    r2t = ReqToTokenPool(n_req, limit, dev)
     # request i, position p -> row 1 + i * max_ctx + p (future decode positions pre-mapped)
-    r2t.req_to_token.copy_(
+    r2t.req_to_token[:, :max_ctx].copy_(
         (1 + torch.arange(n_req, device=dev)[:, None] * max_ctx + torch.arange(max_ctx, device=dev)[None])
         .to(torch.int32))
     backend = B200QuestOnlyBackend(r2t, pool, {"algorithm": "quest", "top_k": TOP_K, "quest_page_size": PAGE})
@@ -692,6 +694,8 @@ def main() -> None:
     ap.add_argument("--requests", type=int, default=N_REQ, help="requests per GPU (profiling cases only)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers (profiling cases only)")
     ap.add_argument("--resident", type=int, default=RESIDENT, help="physical KV buffers")
+    ap.add_argument("--context-limit", type=int, default=None,
+                    help="engine max_context_len above the requests' lengths (profiling cases only)")
     ap.add_argument("--case", choices=["decode", "prefill", "config2", "config3"], default="decode",
                     help="decode: the benchmark, config 1 (default); prefill: the prefill K/V write + bounds; "
                          "config2 / config3: the ragged and HiSparse benchmark configs (1 GPU each)")
@@ -745,7 +749,8 @@ def main() -> None:
     # weak scaling: every rank decodes its own --requests; strong: the batch is sharded by request
     n_req = len(shard_requests([PREFIX + 1] * args.requests, rank, world)) if args.strong else args.requests
     backend, pool, r2t, max_ctx, qkv = build_config1(dev, 3 * total + 1, args.seed + 1000 * rank, n_req=n_req,
-                                                     layers=n_layers, resident=min(args.resident, n_layers))
+                                                     layers=n_layers, resident=min(args.resident, n_layers),
+                                                     context_limit=args.context_limit)
     batches, layers = make_batches(dev, backend, pool, r2t, max_ctx, 3 * total + 1, n_req=n_req)
 
     def barrier():
@@ -879,6 +884,7 @@ def main() -> None:
             "workload": "config1: 64 requests/GPU x 32768-token prefix, 48 layers, Quest top_k 2048 / page 64, "
                         "Qwen3-30B-A3B attention (32q/4kv x 128, bf16), quest mode",
             "requests_per_gpu": n_req, "layers": n_layers, "resident_kv_layers": min(args.resident, n_layers),
+            "context_limit": int(r2t.max_context_len),
             "l2": "inputs larger than L2 (each layer-step reads ~338 MB of distinct data)",
             "layer_step_bytes": step_bytes,
             "layer_step_gbs": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 1e9,

@@ -3,8 +3,8 @@
 //
 // Persistent: one 512-thread block per SM (at most), walking work units with
 // a stride of the grid.  A unit is one part of one request's pages: with a
-// small batch a request is split into `parts` page ranges so that every SM
-// streams bounds.  Within a unit each warp streams its own pages (page
+// small batch a request's candidate pages are split evenly into `parts`
+// ranges so that every SM streams bounds.  Within a unit each warp streams its own pages (page
 // pg0 + warp + 16 m): lane l takes 16-byte words l, l + 32, ... of a page
 // (four channels' (min, max) pairs each) so that its q̄ values stay in
 // registers, and the sign of q̄ picks max or min by a byte permute.  For
@@ -57,7 +57,7 @@ struct SelectArgs {
   int64_t nt_dst_num_rows;
   int32_t* counters;
   uint64_t* lists;  // per-part top-32 lists (workspace)
-  int pages;      // page slots per request covered by the parts (max_pages, or num_pages)
+  int pages;      // page slots per request (max_pages, or num_pages): bounds the number of parts
   int parts;      // units per request: part j takes pages [j * pages / parts, (j + 1) * pages / parts)
   int units;      // bs * parts
   int score_all;  // page_scores API: score pages [0, num_pages) of every request, no selection
@@ -354,8 +354,10 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
       C = st.avoid_recent_overlap ? (F > 0 ? F - 1 : 0) : F;
       is_long = L > st.top_k;
     }
-    const int64_t pg0 = (int64_t)j * a.pages / a.parts, pg1 = (int64_t)(j + 1) * a.pages / a.parts;
-    const int64_t p_end = is_long ? min(pg1, C) : pg0;  // candidate pages of this part: [pg0, p_end)
+    // candidate pages of this part: [pg0, p_end), an even split of the request's own candidates
+    // (not of its page slots, which a long context limit would leave mostly to part 0)
+    const int64_t pg0 = is_long ? (int64_t)j * C / a.parts : 0;
+    const int64_t p_end = is_long ? (int64_t)(j + 1) * C / a.parts : 0;
     float* scores = a.scores + (int64_t)i * st.max_pages;
     const uint4* bounds = reinterpret_cast<const uint4*>(st.page_bounds) +
                           ((size_t)a.layer * st.max_reqs + req) * st.max_pages * page_words;
@@ -502,10 +504,8 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     }
     if (a.score_all) continue;
     // pages that are complete but not candidates read -inf (quest.py:450-451)
-    if (is_long) {
-      const int64_t m0 = max(pg0, C), m1 = min(F, pg1);
-      for (int64_t p = m0 + tid; p < m1; p += kThreads) scores[p] = -__int_as_float(0x7f800000);
-    }
+    if (is_long && j == a.parts - 1)
+      for (int64_t p = C + tid; p < F; p += kThreads) scores[p] = -__int_as_float(0x7f800000);
 
     const int sel = is_long ? (int)min((int64_t)sel_req, C) : 0;
     if (lists) {
