@@ -129,7 +129,8 @@ class _ExtendPlan:
     batch: object
     reqs: list[int]
     seq_lens: list[int]
-    tensors: tuple  # device int64 tensors the struct points into
+    reqs_dev: torch.Tensor  # device int64 [bs]
+    tensors: tuple  # every device tensor the struct points into (kept alive with it)
     qq: _lib.QQExtendBatch
     unfused: bool = False
     admission: object = None
@@ -238,7 +239,7 @@ class _QuestDecodeMixin:
             raise ValueError(f"extend batch: {loc.numel()} out_cache_loc rows for {sum(new_h)} new tokens")
         qq = _lib.QQExtendBatch(reqs.data_ptr(), seq.data_ptr(), prefix.data_ptr(), offsets.data_ptr(),
                                 loc.data_ptr(), loc.numel(), len(seq_h), max(seq_h, default=0))
-        plan = _ExtendPlan(batch, [int(x) for x in reqs.tolist()], seq_h, (reqs, seq, prefix, offsets, loc), qq)
+        plan = _ExtendPlan(batch, [int(x) for x in reqs.tolist()], seq_h, reqs, (reqs, seq, prefix, offsets, loc), qq)
         self._xplan = plan
         return plan
 
@@ -366,7 +367,7 @@ class B200QuestOnlyBackend(_QuestDecodeMixin, AttentionBackend):
             self._extend_write(k, v, li, plan)
             out = self._extend_attention(q, layer, batch)
             if li == self.quest.end_layer - 1:
-                self._skip_first_decode_update.index_fill_(0, plan.tensors[0], 1)
+                self._skip_first_decode_update.index_fill_(0, plan.reqs_dev, 1)
             return out
         plan.unfused = True
         out = super().forward_extend(q, k, v, layer, batch)
