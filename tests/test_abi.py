@@ -55,6 +55,31 @@ def test_argument_errors_are_reported_without_touching_a_device(lib):
         _lib.check(_lib.QQ_ERR_INVALID, "probe")
 
 
+def test_extend_argument_errors_are_reported_without_touching_a_device(lib):
+    """qq_quest_extend_kv checks its arguments before any CUDA call (fake, never dereferenced pointers)."""
+    ok, inv, uns = _lib.QQ_OK, _lib.QQ_ERR_INVALID, _lib.QQ_ERR_UNSUPPORTED
+    table = _lib.QQTokenTable(0x10000, 64)
+
+    def call(st, eb, k=0x20000, v=0x30000, dtype=_lib.QQ_BF16, row=512, src_stride=512, pool_rows=100,
+             tbl=table, hot=None):
+        return lib.qq_quest_extend_kv(st, 0, 0, eb, tbl, k, v, dtype, row, src_stride, 0x40000, 0x50000,
+                                      row, pool_rows, hot, None, None)
+
+    eb = _lib.QQExtendBatch(0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 8, 1, 8)
+    assert call(None, None) == inv                                   # no batch
+    assert call(None, _lib.QQExtendBatch()) == ok                    # empty batch: nothing to do
+    assert call(None, eb, dtype=7) == inv                            # unknown dtype
+    assert call(None, eb, tbl=None) == inv                           # prefix rows need req_to_token
+    assert call(None, eb, tbl=_lib.QQTokenTable(0x10000, 4)) == inv  # table narrower than max_seq_len
+    assert call(None, eb, src_stride=256) == inv                     # rows overlap
+    assert call(None, eb, pool_rows=0) == inv
+    assert call(None, eb, k=0x20002, v=0x30002) == uns               # rows neither 16- nor 4-byte aligned
+    st = _lib.QQQuestState(0x1, 0x2, 0x3, 0x4, 0x5, 2, 4, 8, 2, 64, 16, 64, 0)
+    assert call(st, eb) == inv                                       # 2 x 64 channels, rows of 512
+    hot = _lib.QQHotBuffer(0x60000, None, 512, 128, 100)
+    assert call(None, eb, hot=hot) == inv                            # hot buffer without V
+
+
 def test_device_error_bits_map_to_reference_exceptions():
     with pytest.raises(RuntimeError):
         _lib.raise_device_error(_lib.QQ_DEV_ERR_CAPACITY)
