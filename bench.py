@@ -19,6 +19,14 @@ scaled per channel by LogNormal(0, 0.5)); no dataset exists for this path.
 
 ``--impl reference`` times the CPU oracle (the reference algorithm restated in
 numpy) on the host cores on a bounded sample of the same workload.
+
+Other single-GPU cases, each printing its own JSON line (not the headline):
+``--case prefill`` (one 32K-token prefill's K/V write + Quest bounds over 48
+layers, fused against the reference's order), ``--case config2`` (16 ragged
+requests up to 131K tokens, Mode 2) and ``--case config3`` (HiSparse, 32
+requests at 65,536 tokens with the host tier, against the host-link
+roofline).  ``--context-limit`` runs config 1 under a larger engine
+``max_context_len``.
 Multi-GPU: one process per GPU (torchrun); requests are sharded per GPU with
 no collective on the hot path (weak scaling: 64 requests per GPU).
 """
