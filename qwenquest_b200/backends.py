@@ -251,8 +251,11 @@ class _QuestDecodeMixin:
         n = k.shape[0]
         kk = k.to(k_buf.dtype).reshape(n, dim)
         vv = v.to(v_buf.dtype).reshape(n, dim)
-        if kk.stride(1) != 1 or vv.stride(1) != 1 or kk.stride(0) != vv.stride(0):
-            kk, vv = kk.contiguous(), vv.contiguous()
+        esize = kk.element_size()
+        if (kk.stride(1) != 1 or vv.stride(1) != 1 or kk.stride(0) != vv.stride(0)
+                or (kk.stride(0) * esize) % 4 or kk.data_ptr() % 4 or vv.data_ptr() % 4):
+            # the kernel moves 4- or 16-byte words: fresh contiguous copies are aligned
+            kk, vv = kk.contiguous().clone(), vv.contiguous().clone()
         in_quest = q.start_layer <= layer_id < q.end_layer
         rc = self.lib.qq_quest_extend_kv(
             q._state if in_quest else None, layer_id - q.start_layer, int(layer_id == q.end_layer - 1),
@@ -263,8 +266,13 @@ class _QuestDecodeMixin:
         check(rc, "prefill K/V write")
 
     def _extend_fusable(self) -> bool:
+        """The one-launch prefill write takes bf16 / fp32 pools whose rows are a multiple of 4 bytes."""
         pool = self.token_to_kv_pool
-        return self.fused_extend and pool.dtype in (torch.bfloat16, torch.float32)
+        if not self.fused_extend or pool.dtype not in (torch.bfloat16, torch.float32):
+            return False
+        k_buf = pool.get_key_buffer(self.quest.start_layer)
+        row_bytes = self.quest.kv_heads * self.quest.head_dim * k_buf.element_size()
+        return row_bytes % 4 == 0 and (k_buf.stride(0) * k_buf.element_size()) % 4 == 0
 
     def synchronize(self) -> None:
         """Wait for this backend's work and raise any device error it reported."""

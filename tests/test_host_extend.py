@@ -84,3 +84,31 @@ def test_inconsistent_batches_raise_before_any_launch(case):
         batch = _batch([0], prefix=[5], new=[-1], seq=[4], n_loc=0)
     with pytest.raises(ValueError):
         be._extend_plan(batch)
+
+
+class _FakePool:
+    def __init__(self, dtype, kv, d):
+        self.dtype = dtype
+        self._k = torch.zeros((4, kv, d), dtype=dtype)
+
+    def get_key_buffer(self, layer):
+        return self._k
+
+
+@pytest.mark.parametrize(("dtype", "kv", "d", "fusable"), [
+    (torch.bfloat16, 4, 128, True),
+    (torch.float32, 1, 33, True),      # 132-byte rows: the 4-byte path
+    (torch.bfloat16, 2, 34, True),     # 136-byte rows: the 4-byte path
+    (torch.bfloat16, 1, 33, False),    # 66-byte rows: the reference's order
+    (torch.float16, 4, 128, False),    # a pool dtype the kernel does not take
+])
+def test_fused_prefill_write_only_for_geometries_the_kernel_takes(dtype, kv, d, fusable):
+    from types import SimpleNamespace
+
+    be = _bare_backend()
+    be.fused_extend = True
+    be.token_to_kv_pool = _FakePool(dtype, kv, d)
+    be.quest = SimpleNamespace(start_layer=0, kv_heads=kv, head_dim=d)
+    assert be._extend_fusable() is fusable
+    be.fused_extend = False
+    assert be._extend_fusable() is False
