@@ -27,8 +27,10 @@ requests up to 131K tokens, Mode 2) and ``--case config3`` (HiSparse, 32
 requests at 65,536 tokens with the host tier, against the host-link
 roofline).  ``--context-limit`` runs config 1 under a larger engine
 ``max_context_len``.
-Multi-GPU: one process per GPU (torchrun); requests are sharded per GPU with
-no collective on the hot path (weak scaling: 64 requests per GPU).
+Multi-GPU: one process per GPU (torchrun); config 1's 64 requests are sharded
+in contiguous blocks over the GPUs (64/N per GPU) with no collective on the
+hot path (strong scaling, the configuration the benchmark names); ``--weak``
+gives every GPU its own 64 requests instead.
 """
 
 from __future__ import annotations
@@ -48,6 +50,9 @@ import torch
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+from tests._reference import ensure_importable  # noqa: E402  (the backends plug into the reference package)
+
+ensure_importable()
 
 H, KV, D = 32, 4, 128
 TOP_K, PAGE = 2048, 64
@@ -162,8 +167,8 @@ class _Pool:
 def build_config1(dev, total_steps: int, seed: int, n_req: int = N_REQ, prefix: int = PREFIX,
                   layers: int = LAYERS, resident: int = RESIDENT, context_limit: int | None = None):
     from qwenquest_b200.backends import B200QuestOnlyBackend
-    from qwenquest_b200.memory import ReqToTokenPool
-    from qwenquest_b200.workloads import fill_rows_normal_, torch_generator
+    from qwenquest.memory import ReqToTokenPool
+    from tests.workloads import fill_rows_normal_, torch_generator
 
     max_ctx = ((prefix + total_steps + 1 + PAGE - 1) // PAGE) * PAGE
     rows = n_req * max_ctx + 1
@@ -209,7 +214,7 @@ def build_config1(dev, total_steps: int, seed: int, n_req: int = N_REQ, prefix: 
 def make_batches(dev, backend, pool, r2t, max_ctx, total_steps, n_req=N_REQ, prefix=PREFIX):
     from types import SimpleNamespace
 
-    from qwenquest_b200.batch import ForwardBatch, ForwardMode
+    from qwenquest.batch import ForwardBatch, ForwardMode
 
     reqs = torch.arange(n_req, dtype=torch.int64, device=dev)
     batches = []
@@ -251,8 +256,8 @@ def prefill_case(args) -> None:
     rotate over the layers, so each launch reads beyond L2.
     """
     from qwenquest_b200.backends import B200QuestOnlyBackend
-    from qwenquest_b200.batch import ForwardBatch, ForwardMode
-    from qwenquest_b200.memory import ReqToTokenPool
+    from qwenquest.batch import ForwardBatch, ForwardMode
+    from qwenquest.memory import ReqToTokenPool
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -382,9 +387,9 @@ def config2_case(args) -> None:
     from types import SimpleNamespace
 
     from qwenquest_b200.backends import B200QuestOnlyBackend
-    from qwenquest_b200.batch import ForwardBatch, ForwardMode
-    from qwenquest_b200.memory import ReqToTokenPool
-    from qwenquest_b200.workloads import torch_generator
+    from qwenquest.batch import ForwardBatch, ForwardMode
+    from qwenquest.memory import ReqToTokenPool
+    from tests.workloads import torch_generator
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -487,9 +492,9 @@ def config3_case(args) -> None:
     from types import SimpleNamespace
 
     from qwenquest_b200.backends import B200QuestHiSparseBackend
-    from qwenquest_b200.batch import ForwardBatch, ForwardMode
-    from qwenquest_b200.memory import MHATokenToKVPool, ReqToTokenPool
-    from qwenquest_b200.workloads import fill_rows_normal_, torch_generator
+    from qwenquest.batch import ForwardBatch, ForwardMode
+    from qwenquest.memory import MHATokenToKVPool, ReqToTokenPool
+    from tests.workloads import fill_rows_normal_, torch_generator
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -707,8 +712,8 @@ def main() -> None:
     ap.add_argument("--case", choices=["decode", "prefill", "config2", "config3"], default="decode",
                     help="decode: the benchmark, config 1 (default); prefill: the prefill K/V write + bounds; "
                          "config2 / config3: the ragged and HiSparse benchmark configs (1 GPU each)")
-    ap.add_argument("--strong", action="store_true",
-                    help="shard --requests over the GPUs (strong scaling) instead of --requests per GPU")
+    ap.add_argument("--weak", action="store_true",
+                    help="--requests per GPU (weak scaling) instead of sharding --requests over the GPUs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.case != "decode":
@@ -735,7 +740,8 @@ def main() -> None:
         line = {
             "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * LAYERS / value,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
+            "dtype": "bf16",
             "data": "synthetic", "cpu_baseline": cb,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "config": {"workload": "config1: 64 req x 32768 ctx, 48 layers, Quest top_k 2048 / page 64",
@@ -754,8 +760,8 @@ def main() -> None:
     # three passes of the timed steps: value (inputs resident), per-kernel
     # events (inputs resident) and e2e (host inputs)
     n_layers = args.layers
-    # weak scaling: every rank decodes its own --requests; strong: the batch is sharded by request
-    n_req = len(shard_requests([PREFIX + 1] * args.requests, rank, world)) if args.strong else args.requests
+    # strong scaling (default): the --requests batch is sharded by request; weak: every rank decodes its own
+    n_req = args.requests if args.weak else len(shard_requests([PREFIX + 1] * args.requests, rank, world))
     backend, pool, r2t, max_ctx, qkv = build_config1(dev, 3 * total + 1, args.seed + 1000 * rank, n_req=n_req,
                                                      layers=n_layers, resident=min(args.resident, n_layers),
                                                      context_limit=args.context_limit)
@@ -867,7 +873,7 @@ def main() -> None:
     ms, e2e_ms = max_over_ranks([ms, e2e_ms], device=dev)  # the box is as fast as its slowest GPU
 
     c = PREFIX // PAGE + 0  # candidate pages at the first timed step (F = 512 while seq_len < 32832)
-    batches_per_layer_step = 1 if args.strong else world  # 64-request batches the box decodes per layer step
+    batches_per_layer_step = world if args.weak else 1  # 64-request batches the box decodes per layer step
     value = batches_per_layer_step * n_layers * args.steps / (ms / 1e3)
     e2e_value = batches_per_layer_step * n_layers * args.steps / (e2e_ms / 1e3)
     peak, peak_kind = measured_peaks()
@@ -884,16 +890,22 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": ms / args.steps,
         "higher_is_better": True,
-        "scaling": "strong" if args.strong else "weak",
+        "scaling": "weak" if args.weak else "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) x LogNormal(0,0.5) per-channel K/V, N(0,1) q)",
         "config": {
-            "workload": "config1: 64 requests/GPU x 32768-token prefix, 48 layers, Quest top_k 2048 / page 64, "
+            "workload": (f"config1: {args.requests} requests/GPU" if args.weak else
+                         f"config1: {args.requests} requests sharded over {world} GPU(s)")
+                        + " x 32768-token prefix, 48 layers, Quest top_k 2048 / page 64, "
                         "Qwen3-30B-A3B attention (32q/4kv x 128, bf16), quest mode",
             "requests_per_gpu": n_req, "layers": n_layers, "resident_kv_layers": min(args.resident, n_layers),
             "context_limit": int(r2t.max_context_len),
-            "l2": "inputs larger than L2 (each layer-step reads ~338 MB of distinct data)",
+            "l2": f"inputs larger than L2 (each GPU's layer-step reads ~{step_bytes / 1e6:.0f} MB of distinct data)"
+                  if step_bytes > 126e6 else
+                  f"each GPU's layer-step reads ~{step_bytes / 1e6:.0f} MB of distinct data; the 4 resident KV "
+                  f"buffers rotate over the layers, so a buffer returns after 4 layer-steps "
+                  f"(~{4 * step_bytes / 1e6:.0f} MB of distinct data in between)",
             "layer_step_bytes": step_bytes,
             "layer_step_gbs": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 1e9,
             "layer_step_frac_of_peak": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 1e9 / peak,

@@ -1,7 +1,7 @@
-"""Runs a :class:`qwenquest_b200.workloads.Scenario` through the numpy oracle — test infrastructure only.
+"""Runs a :class:`tests.workloads.Scenario` through the numpy oracle — test infrastructure only.
 
 Same schedule as ``Engine.generate`` (``src/qwenquest/engine.py:143-256``) and
-as :class:`qwenquest_b200.harness.LifecycleDriver`: slot allocation from a
+as :class:`tests.harness.LifecycleDriver`: slot allocation from a
 free list (``memory.py:39-50``), token-pool allocation (``memory.py:53-76``),
 prefill writes + bounds / admission, batched decode, finish.
 """
@@ -14,8 +14,8 @@ import numpy as np
 
 from oracle.backends import OracleKVPools, OracleQuestHiSparseBackend, OracleQuestOnlyBackend
 from oracle.parity import score_pages_f64
-from qwenquest_b200.harness import DecodeRecord
-from qwenquest_b200.workloads import Scenario, scenario_tensors
+from tests.harness import DecodeRecord
+from tests.workloads import Scenario, scenario_tensors
 
 
 class OracleLifecycleDriver:

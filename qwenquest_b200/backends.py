@@ -27,97 +27,25 @@ last layer.
 
 from __future__ import annotations
 
-from abc import ABC, abstractmethod
 from dataclasses import dataclass
 
 import torch
-import torch.nn.functional as F
+from qwenquest.attention.base import AttentionBackend
+from qwenquest.attention.ops import extend_attention
+from qwenquest.config import parse_hisparse_config
 
 from qwenquest_b200 import _lib
 from qwenquest_b200._lib import QQ_STEP_FINALIZE, QQ_STEP_FOLD, check
-from qwenquest_b200.config import avoid_recent_overlap, parse_hisparse_config
 from qwenquest_b200.hisparse import HiSparseCoordinator, _DeviceError
 from qwenquest_b200.quest import QuestAlgorithm, dtype_code, stream_of
 
-__all__ = ["AttentionBackend", "B200QuestHiSparseBackend", "B200QuestOnlyBackend", "extend_attention"]
-
-
-def extend_attention(q, k, v, prefix_len: int, scaling: float) -> torch.Tensor:
-    """Dense causal attention of one request's new tokens (semantics of ``attention/ops.py:18-45``)."""
-    n, num_heads, head_dim = q.shape
-    kv_len, kv_heads, _ = k.shape
-    group = num_heads // kv_heads
-    qh = q.transpose(0, 1).unsqueeze(0)
-    kh = k.repeat_interleave(group, dim=1).transpose(0, 1).unsqueeze(0)
-    vh = v.repeat_interleave(group, dim=1).transpose(0, 1).unsqueeze(0)
-    if prefix_len == 0 and n == kv_len:
-        out = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=scaling)
-    else:
-        q_pos = prefix_len + torch.arange(n, device=q.device)
-        mask = torch.arange(kv_len, device=q.device).unsqueeze(0) <= q_pos.unsqueeze(1)
-        out = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask, scale=scaling)
-    return out[0].transpose(0, 1).reshape(n, num_heads * head_dim)
-
-
-class AttentionBackend(ABC):
-    """The interface of ``attention/base.py:20-112``."""
-
-    name: str = ""
-    uses_token_pool_for_decode: bool = True
-    frees_prefill_kv_after_admission: bool = False
-
-    def __init__(self, req_to_token_pool, token_to_kv_pool):
-        self.req_to_token_pool = req_to_token_pool
-        self.token_to_kv_pool = token_to_kv_pool
-
-    @property
-    def req_to_token(self) -> torch.Tensor:
-        return self.req_to_token_pool.req_to_token
-
-    def init_forward_metadata(self, batch) -> None:  # noqa: B027 - optional hook
-        """Per-forward preparation (once, before layer 0)."""
-
-    def forward(self, q, k, v, layer, batch) -> torch.Tensor:
-        if batch.forward_mode.is_decode():
-            return self.forward_decode(q, k, v, layer, batch)
-        return self.forward_extend(q, k, v, layer, batch)
-
-    def forward_extend(self, q, k, v, layer, batch) -> torch.Tensor:
-        """Dense causal prefill: save the new K/V, then attend per request (base.py:65-93)."""
-        assert batch.out_cache_loc is not None
-        assert batch.extend_prefix_lens is not None
-        self.token_to_kv_pool.set_kv_buffer(layer.layer_id, batch.out_cache_loc, k, v)
-        return self._extend_attention(q, layer, batch)
-
-    def _extend_attention(self, q, layer, batch) -> torch.Tensor:
-        """The attention half of ``forward_extend``, over the K/V rows already in the pool."""
-        k_buf, v_buf = self.token_to_kv_pool.get_kv_buffer(layer.layer_id)
-        offsets = batch.extend_token_offsets()
-        outputs = []
-        for i in range(batch.batch_size):
-            req = int(batch.req_pool_indices[i])
-            seq_len = int(batch.seq_lens[i])
-            locs = self.req_to_token[req, :seq_len].long()
-            outputs.append(
-                extend_attention(q[offsets[i] : offsets[i + 1]], k_buf[locs], v_buf[locs],
-                                 prefix_len=int(batch.extend_prefix_lens[i]), scaling=layer.scaling)
-            )
-        return torch.cat(outputs, dim=0)
-
-    @abstractmethod
-    def forward_decode(self, q, k, v, layer, batch) -> torch.Tensor:
-        """``q``: ``[bs, H, D]``; ``k``/``v``: ``[bs, KV, D]`` of the new tokens -> ``[bs, H*D]``."""
-
-    def on_extend_finished(self, batch) -> None:  # noqa: B027 - optional hook
-        """Called by the engine after a whole prefill forward (all layers)."""
-
-    def on_request_finished(self, req_pool_idx: int) -> None:  # noqa: B027 - optional hook
-        """Called by the engine before a request slot is reused."""
+__all__ = ["B200QuestHiSparseBackend", "B200QuestOnlyBackend"]
 
 
 def _parse_quest_config(sparse_config):
+    """The reference's own parsing and check (``quest_only.py:52-54``)."""
     cfg = parse_hisparse_config(sparse_config)
-    if getattr(cfg, "algorithm", None) != "quest" or getattr(cfg, "quest_page_size", None) is None:
+    if cfg.algorithm != "quest" or cfg.quest_page_size is None:
         raise ValueError("Quest backends require hisparse_config with algorithm='quest'")
     return cfg
 
@@ -141,6 +69,19 @@ class _QuestDecodeMixin:
 
     quest: QuestAlgorithm
     device: torch.device
+
+    def _extend_attention(self, q, layer, batch) -> torch.Tensor:
+        """The attention half of the reference's ``forward_extend`` (``base.py:71-93``), over the K/V rows
+        already in the pool: dense causal prefill through the reference's own ``extend_attention``."""
+        k_buf, v_buf = self.token_to_kv_pool.get_kv_buffer(layer.layer_id)
+        offsets = batch.extend_token_offsets()
+        outputs = []
+        for i in range(batch.batch_size):
+            req = int(batch.req_pool_indices[i])
+            locs = self.req_to_token[req, :int(batch.seq_lens[i])].long()
+            outputs.append(extend_attention(q[offsets[i]:offsets[i + 1]], k_buf[locs], v_buf[locs],
+                                            prefix_len=int(batch.extend_prefix_lens[i]), scaling=layer.scaling))
+        return torch.cat(outputs, dim=0)
 
     def _setup_decode(self, max_reqs: int) -> None:
         dev = self.device
@@ -330,7 +271,7 @@ class B200QuestOnlyBackend(_QuestDecodeMixin, AttentionBackend):
         if self.device.type != "cuda":
             raise ValueError("B200QuestOnlyBackend needs the KV pool on a CUDA device")
         self.quest = QuestAlgorithm(top_k=cfg.top_k, page_size=cfg.quest_page_size, device=self.device,
-                                    avoid_recent_overlap=avoid_recent_overlap(cfg))
+                                    avoid_recent_overlap=cfg.avoid_recent_overlap)
         self.device = self.quest.device
         self.quest.init_storage(
             start_layer=start_layer,
@@ -456,7 +397,7 @@ class B200QuestHiSparseBackend(_QuestDecodeMixin, AttentionBackend):
             raise ValueError("B200QuestHiSparseBackend needs the KV pool on a CUDA device")
         num_layers = token_to_kv_pool.num_layers
         self.quest = QuestAlgorithm(top_k=cfg.top_k, page_size=cfg.quest_page_size, device=self.device,
-                                    avoid_recent_overlap=avoid_recent_overlap(cfg))
+                                    avoid_recent_overlap=cfg.avoid_recent_overlap)
         self.device = self.quest.device
         self.quest.init_storage(
             start_layer=start_layer,
@@ -547,15 +488,3 @@ class B200QuestHiSparseBackend(_QuestDecodeMixin, AttentionBackend):
         self.check_errors()
         self.coord.request_finished(req_pool_idx)
 
-
-def _register_with_reference() -> None:
-    """Make ``isinstance(b, qwenquest...AttentionBackend)`` true when the reference is installed."""
-    try:
-        from qwenquest.attention.base import AttentionBackend as RefBackend  # type: ignore
-    except Exception:
-        return
-    for cls in (B200QuestOnlyBackend, B200QuestHiSparseBackend):
-        RefBackend.register(cls)
-
-
-_register_with_reference()

@@ -22,9 +22,9 @@ host (its host-row free list), so it is not captured.
 from __future__ import annotations
 
 import torch
+from qwenquest.batch import ForwardBatch, ForwardMode
 
 from .backends import B200QuestOnlyBackend
-from .batch import ForwardBatch, ForwardMode
 
 __all__ = ["DecodeStepGraph"]
 

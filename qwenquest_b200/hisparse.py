@@ -27,7 +27,7 @@ import torch
 
 from qwenquest_b200 import _lib
 from qwenquest_b200._lib import QQ_STEP_FINALIZE, QQ_STEP_FOLD, check
-from qwenquest_b200.memory import TokenToKVPoolAllocator
+from qwenquest.memory import TokenToKVPoolAllocator
 from qwenquest_b200.quest import QuestAlgorithm, dtype_code, stream_of
 
 __all__ = ["HiSparseCoordinator", "SwapInStats"]

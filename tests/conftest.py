@@ -9,6 +9,14 @@ REPO = Path(__file__).resolve().parents[1]
 if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 
+from tests import _reference  # noqa: E402
+
+if not _reference.available():
+    import __graft_entry__  # noqa: E402
+
+    __graft_entry__.install_reference()
+_reference.ensure_importable()
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) — run with -m gpu")

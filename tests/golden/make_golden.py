@@ -1,13 +1,14 @@
 """Generate the golden fixtures from the reference implementation itself.
 
-Run in a container where the reference source is available (it is pure
-Python + torch, CPU only)::
+Run where the reference package ``qwenquest`` is importable (it is pure
+Python + torch, CPU only; ``tests._reference`` finds an install under
+``baseline/_ref`` or the directory ``QWENQUEST_REF`` names)::
 
-    python tests/golden/make_golden.py /path/to/QwenQuest/src
+    python tests/golden/make_golden.py [scenario names...]
 
 For every entry of ``scenarios.GOLDEN`` it drives the reference's
 ``QuestOnlyBackend`` / ``QuestHiSparseBackend`` (``src/qwenquest/attention``)
-through :class:`qwenquest_b200.harness.LifecycleDriver` on CPU with the
+through :class:`tests.harness.LifecycleDriver` on CPU with the
 reference's own pools, ``ForwardBatch`` and ``QuestTrace``, and writes per
 (step, layer, request): the selected positions in attention order, the
 attention output, and for HiSparse the hot-buffer state (``buffer_tokens``,
@@ -29,28 +30,14 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
 sys.path.insert(0, str(REPO))
 
-from qwenquest_b200.harness import LifecycleAPI, LifecycleDriver, records_to_arrays  # noqa: E402
 from tests.golden.scenarios import GOLDEN, fixture_name  # noqa: E402
-
-
-def reference_api(src: str) -> LifecycleAPI:
-    sys.path.insert(0, src)
-    from qwenquest.attention import QuestHiSparseBackend, QuestOnlyBackend
-    from qwenquest.batch import ForwardBatch, ForwardMode
-    from qwenquest.memory import MHATokenToKVPool, ReqToTokenPool, TokenToKVPoolAllocator
-    from qwenquest.quest import QuestTrace
-
-    return LifecycleAPI(
-        ForwardBatch, ForwardMode, ReqToTokenPool, MHATokenToKVPool, TokenToKVPoolAllocator,
-        QuestOnlyBackend, QuestHiSparseBackend, QuestTrace,
-    )
+from tests.harness import LifecycleDriver, records_to_arrays, reference_api  # noqa: E402
 
 
 def main(argv: list[str]) -> None:
-    src = argv[1] if len(argv) > 1 else "/root/reference/src"
-    api = reference_api(src)
+    api = reference_api()
     torch.set_num_threads(max(1, torch.get_num_threads()))
-    only = set(argv[2:])
+    only = set(argv[1:])
     for sc, mode, prefill in GOLDEN:
         if only and sc.name not in only:
             continue

@@ -3,12 +3,12 @@
 ``make_golden.py`` (beside this file) runs each scenario through the
 reference's own backends on CPU and stores what they decided; the tests
 regenerate the same seeded inputs with
-:func:`qwenquest_b200.workloads.scenario_tensors`.
+:func:`tests.workloads.scenario_tensors`.
 """
 
 from __future__ import annotations
 
-from qwenquest_b200.workloads import Scenario
+from tests.workloads import Scenario
 
 # The budget the reference's engine tests use (tests/test_engine.py:13), the
 # tiny model geometry (8 q heads / 2 KV heads / head_dim 16, fp32) and its

@@ -1,7 +1,7 @@
 """A model-free serving loop that drives an ``AttentionBackend`` through its lifecycle.
 
 :class:`LifecycleDriver` plays ``Engine.generate`` (``src/qwenquest/engine.py:143-256``)
-with the model replaced by seeded ``q/k/v`` (:func:`qwenquest_b200.workloads.scenario_tensors`):
+with the model replaced by seeded ``q/k/v`` (:func:`tests.workloads.scenario_tensors`):
 slot and token-pool allocation, prefill forwards, ``on_extend_finished``,
 batched decode forwards with ``init_forward_metadata`` once per step, and
 ``on_request_finished`` before a slot is reused.  It only touches the backend
@@ -20,12 +20,15 @@ from typing import Any
 import numpy as np
 import torch
 
-from qwenquest_b200.workloads import Scenario, scenario_tensors
+from tests._reference import ensure_importable
+from tests.workloads import Scenario, scenario_tensors
+
+ensure_importable()
 
 
 @dataclass
 class LifecycleAPI:
-    """The classes a driver needs: the reference's, or this package's mirrors."""
+    """The classes a driver needs: the reference's pools and batch with either backend family."""
 
     ForwardBatch: Any
     ForwardMode: Any
@@ -37,10 +40,25 @@ class LifecycleAPI:
     QuestTrace: Any
 
 
+def reference_api() -> LifecycleAPI:
+    """The reference's own backends, pools, batch and trace (``src/qwenquest``)."""
+    from qwenquest.attention import QuestHiSparseBackend, QuestOnlyBackend
+    from qwenquest.batch import ForwardBatch, ForwardMode
+    from qwenquest.memory import MHATokenToKVPool, ReqToTokenPool, TokenToKVPoolAllocator
+    from qwenquest.quest import QuestTrace
+
+    return LifecycleAPI(
+        ForwardBatch, ForwardMode, ReqToTokenPool, MHATokenToKVPool, TokenToKVPoolAllocator,
+        QuestOnlyBackend, QuestHiSparseBackend, QuestTrace,
+    )
+
+
 def b200_api() -> LifecycleAPI:
+    """The B200 backends and trace with the reference's pools and batch."""
+    from qwenquest.batch import ForwardBatch, ForwardMode
+    from qwenquest.memory import MHATokenToKVPool, ReqToTokenPool, TokenToKVPoolAllocator
+
     from qwenquest_b200.backends import B200QuestHiSparseBackend, B200QuestOnlyBackend
-    from qwenquest_b200.batch import ForwardBatch, ForwardMode
-    from qwenquest_b200.memory import MHATokenToKVPool, ReqToTokenPool, TokenToKVPoolAllocator
     from qwenquest_b200.quest import QuestTrace
 
     return LifecycleAPI(

@@ -9,7 +9,7 @@ from pathlib import Path
 import numpy as np
 
 from oracle.parity import compare_selection
-from qwenquest_b200.harness import DecodeRecord, records_to_arrays
+from tests.harness import DecodeRecord, records_to_arrays
 
 GOLDEN_DIR = Path(__file__).resolve().parent / "golden"
 

@@ -18,8 +18,8 @@ from __future__ import annotations
 
 import pytest
 
-from qwenquest_b200.harness import LifecycleDriver, b200_api, records_to_arrays
-from qwenquest_b200.workloads import Scenario
+from tests.harness import LifecycleDriver, b200_api, records_to_arrays
+from tests.workloads import Scenario
 from tests.parity_helpers import compare_runs, oracle_run
 
 pytestmark = pytest.mark.gpu

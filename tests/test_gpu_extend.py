@@ -27,8 +27,8 @@ import torch
 
 from oracle.quest import OracleQuest
 from qwenquest_b200.backends import B200QuestHiSparseBackend, B200QuestOnlyBackend
-from qwenquest_b200.batch import ForwardBatch, ForwardMode
-from qwenquest_b200.memory import MHATokenToKVPool, ReqToTokenPool
+from qwenquest.batch import ForwardBatch, ForwardMode
+from qwenquest.memory import MHATokenToKVPool, ReqToTokenPool
 
 pytestmark = pytest.mark.gpu
 

@@ -17,8 +17,8 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from qwenquest_b200.harness import LifecycleDriver, b200_api
-from qwenquest_b200.workloads import Scenario
+from tests.harness import LifecycleDriver, b200_api
+from tests.workloads import Scenario
 from tests.test_gpu_configs import CONFIG2_SAMPLE
 
 pytestmark = pytest.mark.gpu

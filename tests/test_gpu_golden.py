@@ -13,7 +13,7 @@ from __future__ import annotations
 
 import pytest
 
-from qwenquest_b200.harness import LifecycleDriver, b200_api, records_to_arrays
+from tests.harness import LifecycleDriver, b200_api, records_to_arrays
 from tests.golden.scenarios import GOLDEN, fixture_name
 from tests.parity_helpers import compare_runs, load_golden, oracle_run
 

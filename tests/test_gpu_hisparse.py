@@ -15,7 +15,7 @@ import pytest
 import torch
 
 from qwenquest_b200.hisparse import HiSparseCoordinator
-from qwenquest_b200.memory import MHATokenToKVPool
+from qwenquest.memory import MHATokenToKVPool
 from qwenquest_b200.quest import QuestAlgorithm
 
 pytestmark = pytest.mark.gpu

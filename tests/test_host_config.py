@@ -1,63 +1,47 @@
-"""Host-side logic (CPU): ``--hisparse-config`` parsing, the workload generator, the lifecycle driver."""
+"""Host-side logic (CPU): the backends' ``--hisparse-config`` handling, the workload generator.
+
+The backends parse their ``sparse_config`` with the reference's own
+``parse_hisparse_config`` (``src/qwenquest/config.py:298-359``) and apply the
+reference backends' Quest check (``attention/quest_only.py:52-54``); these
+tests pin that they accept and reject exactly what the reference does.
+"""
 
 from __future__ import annotations
 
-import sys
-from pathlib import Path
-
 import numpy as np
 import pytest
+from qwenquest.config import SparseConfig, parse_hisparse_config
 
-from qwenquest_b200.config import SparseConfig, avoid_recent_overlap, parse_hisparse_config
-from qwenquest_b200.workloads import Scenario, scenario_tensors
-
-REF_SRC = Path("/root/reference/src")
-
-
-def test_defaults_follow_upstream():
-    cfg = parse_hisparse_config({"algorithm": "quest"})
-    assert (cfg.top_k, cfg.device_buffer_size, cfg.quest_page_size) == (2048, 4096, 64)
-    assert (cfg.host_to_device_ratio, cfg.swap_in_block_size) == (2, 960)
-    assert not avoid_recent_overlap(cfg)
+from qwenquest_b200.backends import _parse_quest_config
+from tests.workloads import Scenario, scenario_tensors
 
 
-def test_unknown_keys_go_to_the_extra_config():
-    cfg = parse_hisparse_config('{"algorithm": "quest", "top_k": 32, "quest_page_size": 8, '
-                                '"avoid_recent_overlap": true, "foo": 1}')
-    assert cfg.sparse_extra_config == {"avoid_recent_overlap": True, "foo": 1}
-    assert avoid_recent_overlap(cfg) and cfg.avoid_recent_overlap
-
-
-@pytest.mark.parametrize("bad", [
-    {"top_k": 100, "algorithm": "quest"},
-    {"top_k": 64, "device_buffer_size": 32},
-    {"swap_in_block_size": 0},
-    {"swap_in_block_size": 2000},
-    {"swap_in_block_size": True},
-    {"algorithm": "quest", "quest_page_size": 0},
-    "{not json",
-])
-def test_invalid_configs_raise_value_error(bad):
-    with pytest.raises(ValueError):
-        parse_hisparse_config(bad)
+@pytest.mark.parametrize("raw", [{"algorithm": "quest"}, '{"algorithm":"quest","top_k":256,"quest_page_size":16}',
+                                 {"algorithm": "quest", "avoid_recent_overlap": True, "device_buffer_size": 8192}])
+def test_quest_configs_parse_as_the_reference_does(raw):
+    cfg = _parse_quest_config(raw)
+    assert isinstance(cfg, SparseConfig)
+    assert cfg == parse_hisparse_config(raw)
+    assert cfg.avoid_recent_overlap == bool(isinstance(raw, dict) and raw.get("avoid_recent_overlap"))
 
 
 def test_parsed_objects_pass_through():
     cfg = SparseConfig(top_k=64, quest_page_size=16, algorithm="quest")
-    assert parse_hisparse_config(cfg) is cfg
+    assert _parse_quest_config(cfg) is cfg
 
 
-@pytest.mark.skipif(not REF_SRC.exists(), reason="reference source not present")
-@pytest.mark.parametrize("raw", [None, {"algorithm": "quest"}, '{"algorithm":"quest","top_k":256,"quest_page_size":16}',
-                                 {"algorithm": "quest", "avoid_recent_overlap": True, "device_buffer_size": 8192}])
-def test_parsing_matches_the_reference(raw):
-    sys.path.insert(0, str(REF_SRC))
-    from qwenquest.config import parse_hisparse_config as ref_parse
-
-    a, b = parse_hisparse_config(raw), ref_parse(raw)
-    for name in ("top_k", "device_buffer_size", "host_to_device_ratio", "swap_in_block_size", "algorithm",
-                 "quest_page_size", "sparse_extra_config", "avoid_recent_overlap"):
-        assert getattr(a, name) == getattr(b, name), name
+@pytest.mark.parametrize("bad", [
+    None,
+    {"top_k": 64},
+    {"top_k": 100, "algorithm": "quest"},
+    {"top_k": 64, "device_buffer_size": 32, "algorithm": "quest"},
+    {"swap_in_block_size": 0, "algorithm": "quest"},
+    {"algorithm": "quest", "quest_page_size": 0},
+    "{not json",
+])
+def test_non_quest_or_invalid_configs_raise_value_error(bad):
+    with pytest.raises(ValueError):
+        _parse_quest_config(bad)
 
 
 def test_scenario_tensors_are_seeded_and_bf16_exact():

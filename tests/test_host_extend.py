@@ -16,7 +16,7 @@ import pytest
 import torch
 
 from qwenquest_b200.backends import B200QuestOnlyBackend
-from qwenquest_b200.batch import ForwardBatch, ForwardMode
+from qwenquest.batch import ForwardBatch, ForwardMode
 
 
 def _bare_backend() -> B200QuestOnlyBackend:
