@@ -712,6 +712,8 @@ def main() -> None:
     ap.add_argument("--case", choices=["decode", "prefill", "config2", "config3"], default="decode",
                     help="decode: the benchmark, config 1 (default); prefill: the prefill K/V write + bounds; "
                          "config2 / config3: the ragged and HiSparse benchmark configs (1 GPU each)")
+    ap.add_argument("--path", choices=["graph", "eager"], default="graph",
+                    help="headline path: the decode step replayed as a CUDA graph (default) or the eager calls")
     ap.add_argument("--weak", action="store_true",
                     help="--requests per GPU (weak scaling) instead of sharding --requests over the GPUs")
     args = ap.parse_args()
@@ -720,6 +722,7 @@ def main() -> None:
         if int(os.environ.get("RANK", "0")) == 0:
             {"prefill": prefill_case, "config2": config2_case, "config3": config3_case}[args.case](args)
         return
+    from qwenquest_b200.graphs import DecodeStepGraph
     from qwenquest_b200.sharding import max_over_ranks, shard_requests
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -757,46 +760,72 @@ def main() -> None:
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     total = args.warmup + args.steps
-    # three passes of the timed steps: value (inputs resident), per-kernel
-    # events (inputs resident) and e2e (host inputs)
+    # five passes of W + K steps each, in this order: eager (the drop-in
+    # forward calls), graph (the same steps replayed as a captured
+    # DecodeStepGraph), per-kernel events (eager, two calls per layer), e2e
+    # through the graph, e2e through the eager calls
     n_layers = args.layers
     # strong scaling (default): the --requests batch is sharded by request; weak: every rank decodes its own
     n_req = args.requests if args.weak else len(shard_requests([PREFIX + 1] * args.requests, rank, world))
-    backend, pool, r2t, max_ctx, qkv = build_config1(dev, 3 * total + 1, args.seed + 1000 * rank, n_req=n_req,
+    n_steps = 5 * total + 2
+    backend, pool, r2t, max_ctx, qkv = build_config1(dev, n_steps, args.seed + 1000 * rank, n_req=n_req,
                                                      layers=n_layers, resident=min(args.resident, n_layers),
                                                      context_limit=args.context_limit)
-    batches, layers = make_batches(dev, backend, pool, r2t, max_ctx, 3 * total + 1, n_req=n_req)
+    batches, layers = make_batches(dev, backend, pool, r2t, max_ctx, n_steps, n_req=n_req)
+    qs, ks, vs = qkv
+    cursor = [0]
+
+    def take(n):
+        first = cursor[0]
+        cursor[0] += n
+        return range(first, first + n)
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
 
-    # ---- value: device-resident inputs, nothing but the step in the timed region
-    for s in range(args.warmup):
-        run_step(backend, batches[s], layers, qkv)
-    barrier()
-    clocks = ClockSampler(dev.index if world == 1 else local_rank)
-    clocks.start()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    torch.cuda.nvtx.range_push("timed_value")  # profilers select the timed steps by this range
-    for s in range(args.warmup, total):
-        run_step(backend, batches[s], layers, qkv)
-    torch.cuda.nvtx.range_pop()
-    end.record()
-    barrier()
-    clock_info = clocks.stop()
-    ms = start.elapsed_time(end)
+    def timed(run, steps, clocks=None):
+        """Device time of `run(s)` over `steps` (CUDA events on the compute stream, a barrier on both sides)."""
+        barrier()
+        if clocks is not None:
+            clocks.start()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        torch.cuda.nvtx.range_push("timed")  # profilers select the timed steps by this range
+        for st in steps:
+            run(st)
+        torch.cuda.nvtx.range_pop()
+        b.record()
+        barrier()
+        info = clocks.stop() if clocks is not None else None
+        return a.elapsed_time(b), info
+
+    eager_step = lambda st: run_step(backend, batches[st], layers, qkv)  # noqa: E731
+
+    # ---- eager: the drop-in calls (init_forward_metadata + forward per layer), inputs resident
+    for st in take(args.warmup):
+        eager_step(st)
+    eager_ms, _ = timed(eager_step, take(args.steps))
     backend.check_errors()
 
-    # ---- per-kernel durations (CUDA events on the launching stream), same steps again
-    for s in range(total, total + args.warmup):
-        run_step(backend, batches[s], layers, qkv)
+    # ---- graph: the same steps as replays of a captured DecodeStepGraph (the headline by default)
+    graph = DecodeStepGraph(backend, layers, batches[cursor[0]], qs, ks, vs)
+    graph_step = lambda st: graph.replay(batches[st])  # noqa: E731
+    for st in take(args.warmup):
+        graph_step(st)
+    clock_dev = dev.index if world == 1 else local_rank
+    graph_ms, clock_info = timed(graph_step, take(args.steps), ClockSampler(clock_dev))
+    backend.check_errors()
+    del graph
+
+    # ---- per-kernel durations (CUDA events on the launching stream), eager two-call path
+    for st in take(args.warmup):
+        eager_step(st)
     barrier()
     backend.kernel_events = {}
-    for s in range(total + args.warmup, 2 * total):
-        run_step(backend, batches[s], layers, qkv)
+    for st in take(args.steps):
+        eager_step(st)
     barrier()
     kev = backend.kernel_events
     backend.kernel_events = None
@@ -809,25 +838,24 @@ def main() -> None:
     # into one of two buffer sets by step parity; the step's outputs behind
     # it), ordered by events, so PCIe traffic overlaps the kernels.  The timed
     # region spans every copy.
-    qs, ks, vs = qkv
     hq, hk, hv = (t.cpu().pin_memory() for t in (qs, ks, vs))
     hout = torch.empty((n_layers, n_req, H * D), dtype=torch.bfloat16).pin_memory()
-    dbuf = [tuple(torch.empty_like(t) for t in (qs, ks, vs)) for _ in range(2)]
-    dout = [torch.empty((n_layers, n_req, H * D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     compute = torch.cuda.current_stream(dev)
     h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-    def e2e_steps(first, last):
-        """Steps [first, last) with their copies; returns with every stream's work queued."""
+    def e2e_pass(bufs, step, steps):
+        """`steps` with their copies: bufs[p] = (q, k, v, out) device buffers of parity p, step(st, p)
+        runs step st on buffer set p; returns once every stream's work is queued."""
         step_done = [None, None]  # compute finished with the buffer set of that parity
         out_done = [None, None]  # the device->host copy finished with the output buffer of that parity
+        steps = list(steps)
 
-        def copy_inputs(s):
-            if step_done[s % 2] is not None:
-                h2d.wait_event(step_done[s % 2])
+        def copy_inputs(i):
+            p = i % 2
+            if step_done[p] is not None:
+                h2d.wait_event(step_done[p])
             with torch.cuda.stream(h2d):
-                for dst, src in zip(dbuf[s % 2], (hq, hk, hv), strict=True):
+                for dst, src in zip(bufs[p][:3], (hq, hk, hv), strict=True):
                     dst.copy_(src, non_blocking=True)
             ev = torch.cuda.Event()
             ev.record(h2d)
@@ -835,47 +863,71 @@ def main() -> None:
 
         h2d.wait_stream(compute)
         d2h.wait_stream(compute)
-        ready = copy_inputs(first)
-        for s in range(first, last):
-            dq, dk, dv = dbuf[s % 2]
-            b = batches[s]
+        ready = copy_inputs(0)
+        for i, st in enumerate(steps):
+            p = i % 2
             compute.wait_event(ready)
-            backend.init_forward_metadata(b)
-            outs = [backend.forward(dq[layer.layer_id], dk[layer.layer_id], dv[layer.layer_id], layer, b)
-                    for layer in layers]
-            if out_done[s % 2] is not None:
-                compute.wait_event(out_done[s % 2])
-            torch.stack(outs, out=dout[s % 2])
+            if out_done[p] is not None:
+                compute.wait_event(out_done[p])
+            step(st, p)
             done = torch.cuda.Event()
             done.record(compute)
-            step_done[s % 2] = done
+            step_done[p] = done
             # the step's outputs cross PCIe (one copy) while the next step computes
             d2h.wait_event(done)
             with torch.cuda.stream(d2h):
-                hout.copy_(dout[s % 2], non_blocking=True)
-            out_done[s % 2] = torch.cuda.Event()
-            out_done[s % 2].record(d2h)
-            if s + 1 < last:
-                ready = copy_inputs(s + 1)  # the next step's inputs cross PCIe during this step
+                hout.copy_(bufs[p][3], non_blocking=True)
+            out_done[p] = torch.cuda.Event()
+            out_done[p].record(d2h)
+            if i + 1 < len(steps):
+                ready = copy_inputs(i + 1)  # the next step's inputs cross PCIe during this step
         compute.wait_stream(d2h)
         compute.wait_stream(h2d)
 
-    e2e_steps(2 * total, 2 * total + args.warmup)  # warm-up: the same steps, copies included
-    barrier()
-    e2e_start.record(compute)
-    t_host = time.perf_counter()
-    e2e_steps(2 * total + args.warmup, 3 * total)
-    e2e_host_ms = 1e3 * (time.perf_counter() - t_host) / args.steps  # enqueue time per step
-    e2e_end.record(compute)
-    barrier()
-    e2e_ms = e2e_start.elapsed_time(e2e_end)
+    def timed_e2e(bufs, step):
+        e2e_pass(bufs, step, take(args.warmup))  # warm-up: the same steps, copies included
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(compute)
+        t_host = time.perf_counter()
+        e2e_pass(bufs, step, take(args.steps))
+        host_ms = 1e3 * (time.perf_counter() - t_host) / args.steps  # enqueue time per step
+        b.record(compute)
+        barrier()
+        return a.elapsed_time(b), host_ms
 
-    ms, e2e_ms = max_over_ranks([ms, e2e_ms], device=dev)  # the box is as fast as its slowest GPU
+    # through two graphs (by step parity), each with its own input and stacked output buffers
+    graphs = [DecodeStepGraph(backend, layers, batches[cursor[0]], qs, ks, vs, stack_outputs=True)
+              for _ in range(2)]
+    gbufs = [(g.q, g.k, g.v, g.out_stacked) for g in graphs]
+    e2e_ms, e2e_host_ms = timed_e2e(gbufs, lambda st, p: graphs[p].replay(batches[st]))
+    backend.check_errors()
+    del graphs, gbufs
+
+    # through the eager calls
+    ebufs = [tuple(torch.empty_like(t) for t in (qs, ks, vs)) +
+             (torch.empty((n_layers, n_req, H * D), dtype=torch.bfloat16, device=dev),) for _ in range(2)]
+
+    def eager_e2e_step(st, p):
+        dq, dk, dv, dout = ebufs[p]
+        b = batches[st]
+        backend.init_forward_metadata(b)
+        torch.stack([backend.forward(dq[lay.layer_id], dk[lay.layer_id], dv[lay.layer_id], lay, b)
+                     for lay in layers], out=dout)
+
+    e2e_eager_ms, e2e_eager_host_ms = timed_e2e(ebufs, eager_e2e_step)
+    backend.check_errors()
+
+    graph_ms, eager_ms, e2e_ms, e2e_eager_ms = max_over_ranks([graph_ms, eager_ms, e2e_ms, e2e_eager_ms],
+                                                              device=dev)  # the box is as fast as its slowest GPU
+    ms, value_path = (graph_ms, "graph") if args.path == "graph" else (eager_ms, "eager")
 
     c = PREFIX // PAGE + 0  # candidate pages at the first timed step (F = 512 while seq_len < 32832)
     batches_per_layer_step = world if args.weak else 1  # 64-request batches the box decodes per layer step
-    value = batches_per_layer_step * n_layers * args.steps / (ms / 1e3)
-    e2e_value = batches_per_layer_step * n_layers * args.steps / (e2e_ms / 1e3)
+    layer_steps = batches_per_layer_step * n_layers * args.steps
+    value = layer_steps / (ms / 1e3)
+    e2e_ms_head, e2e_host_head = (e2e_ms, e2e_host_ms) if value_path == "graph" else (e2e_eager_ms, e2e_eager_host_ms)
+    e2e_value = layer_steps / (e2e_ms_head / 1e3)
     peak, peak_kind = measured_peaks()
     attn_ms = kernel_ms.get("sparse_decode_attention")
     achieved = n_req * ATTN_BYTES_PER_REQ / (attn_ms / 1e3) / 1e9 if attn_ms else None
@@ -910,6 +962,18 @@ def main() -> None:
             "layer_step_gbs": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 1e9,
             "layer_step_frac_of_peak": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 1e9 / peak,
             "kernel_ms": kernel_ms,
+            "path": value_path,
+            "paths": {
+                "graph": {"value": layer_steps / (graph_ms / 1e3), "ms_per_step": graph_ms / args.steps,
+                          "e2e": layer_steps / (e2e_ms / 1e3), "e2e_host_enqueue_ms_per_step": e2e_host_ms,
+                          "what": "DecodeStepGraph.replay per step (the decode step captured once: "
+                                  "fold + 48 x fused selection/attention, device-side epochs)"},
+                "eager": {"value": layer_steps / (eager_ms / 1e3), "ms_per_step": eager_ms / args.steps,
+                          "e2e": layer_steps / (e2e_eager_ms / 1e3),
+                          "e2e_host_enqueue_ms_per_step": e2e_eager_host_ms,
+                          "what": "init_forward_metadata + forward per layer (the drop-in calls Engine.generate "
+                                  "makes), fused selection/attention call per layer"},
+            },
         },
         "roofline": {
             "bound": "hbm",
@@ -929,7 +993,7 @@ def main() -> None:
             "unit": UNIT,
             "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in (hq, hk, hv))),
             "d2h_bytes_per_step": int(hout.numel() * hout.element_size()),
-            "host_enqueue_ms_per_step": e2e_host_ms,
+            "host_enqueue_ms_per_step": e2e_host_head,
         },
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -83,8 +83,10 @@ typedef struct qq_batch {
 
 /* Where a row of the attended pool comes from. */
 typedef struct qq_token_table {
-  const int32_t* req_to_token; /* device [max_reqs][stride] */
+  const int32_t* req_to_token; /* device [rows][stride] */
   int64_t stride;
+  int64_t rows;                /* request rows of the table; a request index outside [0, rows)
+                                  is reported as QQ_DEV_ERR_BOUNDS (0: not checked) */
 } qq_token_table;
 
 /* The new token's K/V write fused into qq_quest_retrieve_topk.
@@ -269,9 +271,9 @@ int qq_sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, 
  * device memory at call time — an engine that reserves all memory before it
  * serves and forbids allocations on its decode path, or a host program that
  * binds this C-ABI without a device allocator of its own.  Its scratch is a
- * fixed array inside the library (9,867,264 bytes per device: arrival
- * counters for QQ_NOALLOC_MAX_BS requests and partial records for a grid of
- * at most 148 blocks).  Fast-path geometry only (bf16, 32 query heads over
+ * fixed array inside the library (11,098,624 bytes per device: arrival
+ * counters for QQ_NOALLOC_MAX_BS requests and partial records of the warps
+ * and blocks of a grid of at most 148 blocks).  Fast-path geometry only (bf16, 32 query heads over
  * 4 KV heads, head_dim 128, top_k a multiple of 16, 16-byte aligned rows
  * and pools) and bs <= QQ_NOALLOC_MAX_BS; anything else returns
  * QQ_ERR_UNSUPPORTED.  The first call on a device, made with that device
@@ -286,6 +288,26 @@ int qq_sparse_decode_attention_noalloc(const qq_batch* batch, int top_k, const v
                                        int64_t kv_row_stride, int64_t num_rows, float scaling,
                                        void* out, int64_t out_stride, uint32_t* err, void* stream);
 
+/* ---- [Q7] attention behind a caller's own producer ------------------- */
+/* qq_sparse_decode_attention that may start before the rows are written: on
+ * the fast path it reads request i's rows once ready[i] == epoch (an acquire
+ * load), for a producer kernel launched just before it on `stream` that
+ * writes the rows and then stores the word with release semantics (as the
+ * selection of qq_quest_decode_attention does).  Each wait gives up after
+ * wait_limit_ns of %globaltimer (0: 2 s), reports QQ_DEV_ERR_TIMEOUT in
+ * `err` and reads the rows as they are; no wait can hang the GPU.  epoch
+ * must not be 0 (a cleared word).  Other geometries run the generic kernel
+ * after the producer, stream-ordered.  No reference counterpart: the
+ * reference attends only after its selection has returned
+ * (quest_only.py:153-158). */
+int qq_sparse_decode_attention_ready(const qq_batch* batch, int top_k, const void* q, int dtype, int q_heads,
+                                     int kv_heads, int head_dim, int64_t q_stride, const int32_t* rows,
+                                     const void* k_pool, const void* v_pool, int64_t kv_row_stride,
+                                     int64_t num_rows, float scaling, void* out, int64_t out_stride,
+                                     uint32_t* err, const uint32_t* ready, uint32_t epoch,
+                                     uint64_t wait_limit_ns, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+
 /* ---- [Q5][Q6][Q7] + [Q7] selection and attention in one call ---------- */
 /* qq_quest_retrieve_topk (with the req_to_token translation into rows)
  * followed by qq_sparse_decode_attention over those rows, q_heads x
@@ -293,8 +315,11 @@ int qq_sparse_decode_attention_noalloc(const qq_batch* batch, int top_k, const v
  * `workspace`.  The results are those of the two calls.  On the attention
  * fast path the attention kernel starts while the selection still runs and
  * reads a request's rows as soon as that request's ready word in the
- * workspace holds this call's epoch (a per-call number the library keeps),
- * so its set-up and the selection's tail overlap.  No reference
+ * workspace holds this call's epoch, so its set-up and the selection's tail
+ * overlap.  The epoch is a call counter kept in the workspace on the device
+ * (the attention's last block advances it), so a call captured in a CUDA
+ * graph gets a fresh epoch on every replay.  A request index outside the
+ * state or the table is reported in `err` (QQ_DEV_ERR_BOUNDS).  No reference
  * counterpart: QuestOnlyBackend.forward_decode makes the two calls in turn
  * (quest_only.py:153-158). */
 int qq_quest_decode_attention(const qq_quest_state* st, int layer, const qq_batch* batch,

@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_DIR = Path(__file__).resolve().parent / "_lib"
@@ -60,7 +60,7 @@ class QQBatch(ctypes.Structure):
 
 
 class QQTokenTable(ctypes.Structure):
-    _fields_ = [("req_to_token", c_void_p), ("stride", c_int64)]
+    _fields_ = [("req_to_token", c_void_p), ("stride", c_int64), ("rows", c_int64)]
 
 
 class QQNewToken(ctypes.Structure):
@@ -149,6 +149,10 @@ SIGNATURES: dict[str, tuple] = {
     "qq_sparse_decode_attention": (
         c_int, [_B, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p,
                 c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "qq_sparse_decode_attention_ready": (
+        c_int, [_B, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p,
+                c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_uint32, c_uint64, c_void_p,
+                c_size_t, c_void_p]),
     "qq_quest_decode_attention": (
         c_int, [_S, c_int, _B, c_void_p, c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p, _T, c_void_p,
                 _N, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p,

@@ -141,7 +141,7 @@ class _QuestDecodeMixin:
         r2t = self.req_to_token
         t = self._r2t_table
         if t is None or t.req_to_token != r2t.data_ptr() or t.stride != r2t.stride(0):
-            t = self._r2t_table = _lib.QQTokenTable(r2t.data_ptr(), r2t.stride(0))
+            t = self._r2t_table = _lib.QQTokenTable(r2t.data_ptr(), r2t.stride(0), r2t.shape[0])
         return t
 
     def check_errors(self) -> None:

@@ -69,28 +69,34 @@ struct AttnArgs {
   void* out;
   int64_t out_stride;
   uint32_t* err;
-  float* part;        // [warps][2][kPartFloats]
-  int32_t* seg_count; // [bs * kKV] arrival counters of split segments
+  float* part;        // [warps][2][kPartFloats]: the warps' records of split segments
+  float* bpart;       // [blocks][2][kPartFloats]: the blocks' records of segments split across blocks
+  int32_t* seg_count; // [bs * kKV] arrival counters (blocks) of segments split across blocks
   // fused selection + attention: rows of request i may be read once
   // ready[i] == epoch (the selection kernel runs ahead); null: the rows
-  // were written before this launch
+  // were written before this launch.  The epoch is *call_counter + 1 (the
+  // last block to exit advances the counter; exit_count: arrivals), or
+  // fixed_epoch without a counter.  A wait gives up after wait_limit_ns.
   const uint32_t* ready;
-  uint32_t epoch;
+  uint32_t* call_counter;
+  int32_t* exit_count;
+  uint32_t fixed_epoch;
+  uint64_t wait_limit_ns;
 };
 
 // Request r's rows are written: lane 0 spins on its ready word (acquire,
 // bounded), the warp barrier orders every lane's later reads after it.
 // `known` is the last request this warp saw ready (warps visit requests in
 // increasing order).
-__device__ __forceinline__ void ensure_ready(const AttnArgs& a, int r, int& known) {
+__device__ __forceinline__ void ensure_ready(const AttnArgs& a, uint32_t epoch, int r, int& known) {
   if (a.ready == nullptr || r == known) return;
   if ((threadIdx.x & 31) == 0) {
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
       uint32_t v;
       asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.ready + r) : "memory");
-      if (v == a.epoch) break;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (v == epoch) break;
+      if (globaltimer_ns() - t0 > a.wait_limit_ns) {
         raise_error(a.err, QQ_DEV_ERR_TIMEOUT);
         break;
       }
@@ -283,9 +289,9 @@ __device__ __forceinline__ void copy_stage(const AttnArgs& a, const Walk& w, Sta
   }
 }
 
-__device__ __forceinline__ void issue_stage(const AttnArgs& a, const Walk& w, const char* lane_pool,
+__device__ __forceinline__ void issue_stage(const AttnArgs& a, uint32_t epoch, const Walk& w, const char* lane_pool,
                                             uint32_t lane_dst, uint32_t stride, uint32_t max_row, int& known) {
-  ensure_ready(a, w.s_req, known);
+  ensure_ready(a, epoch, w.s_req, known);
   StageRows s;
   load_stage_rows(a, w, s);
   copy_stage(a, w, s, lane_pool, lane_dst, stride, max_row);
@@ -299,51 +305,35 @@ struct StreamCfg {
   static constexpr size_t kSmem = kRing + sizeof(int32_t) * (QQ_MAX_BS + 1);
 };
 
+// A segment split across warps, as the block's merge sees it.  A warp's (a
+// block's) record of a segment is in slot 0 when the segment is the first
+// of its share (range), else in slot 1: only the first warp (block) holding
+// a record can have it in slot 1, the others' shares start inside it.
+struct SegTask {
+  int req, head;
+  int wa, wb;     // this block's warps holding records of it
+  int ba, bb;     // blocks holding records of it (ba < bb: it continues beyond this block)
+  int slot_wa;    // slot of warp wa's record
+  int slot_ba;    // slot of block ba's record
+  int slot_here;  // slot of this block's record
+};
+
+// The block's list of split segments to merge, filled while the warps
+// stream: the first of the block's warps that holds a record of a segment
+// adds it when it finishes its portion (at most two per warp).
+constexpr int kMaxTasks = 2 * kAttnWarpsPerSm;
+struct BlockTasks {
+  SegTask task[kMaxTasks];
+  int n;
+};
+
+// One warp's share of the stream-K split: its stages through the warp's ring,
+// whole segments written to the output, split ones as (m, l, O) records.
 template <int WARPS, int SLOTS>
-__global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) {
-  using Cfg = StreamCfg<WARPS, SLOTS>;
-  // behind a fused selection the ready words order the reads instead of the
-  // grid dependency; the selection's own wait keeps earlier grids ahead
-  if (a.ready == nullptr) wait_prior_grid();
-  allow_next_grid();
-  extern __shared__ __align__(128) char smem[];
-  int32_t* s_prefix4 = reinterpret_cast<int32_t*>(smem + Cfg::kRing);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void stream_share(const AttnArgs& a, uint32_t epoch, const Split& sp, int W, char* ring,
+                                             BlockTasks& bt) {
+  const int lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  char* ring = smem + (size_t)warp * SLOTS * kSlotBytes;
-
-  // segment prefix 4 * P_i over the batch (warp 0, 32 requests at a time)
-  if (warp == 0) {
-    int32_t run = 0;
-    for (int b0 = 0; b0 < a.bs; b0 += 32) {
-      const int b = b0 + lane;
-      int32_t n = 0;
-      if (b < a.bs) {
-        const int64_t L = a.seq_lens[b];
-        n = (int32_t)(L < a.top_k ? (L < 0 ? 0 : L) : a.top_k);
-      }
-      int32_t incl = 4 * n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      if (b < a.bs) s_prefix4[b + 1] = run + incl;
-      run += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) s_prefix4[0] = 0;
-  }
-  __syncthreads();
-
-  Split sp;
-  sp.prefix4 = s_prefix4;
-  sp.bs = a.bs;
-  sp.T = s_prefix4[a.bs];
-  if (sp.T == 0) return;
-  const int grid_warps = gridDim.x * WARPS;
-  sp.NW = min(grid_warps, max(1, sp.T / kMinShare));
-  const int W = blockIdx.x * WARPS + warp;
-  if (W >= sp.NW) return;
   const __nv_bfloat16* qbase = static_cast<const __nv_bfloat16*>(a.q);
 
   // per-lane copy constants
@@ -370,7 +360,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       ph[s] = have_f;
       if (have_f) {
         pw[s] = fc;
-        ensure_ready(a, fc.s_req, known);
+        ensure_ready(a, epoch, fc.s_req, known);
         load_stage_rows(a, fc, pr[s]);
         have_f = walk_next(sp, fc);
       }
@@ -406,7 +396,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
     cp_async_wait<SLOTS - 2>();
     __syncwarp();  // the current stage is visible to every lane; the previous stage's slot is free
     if (have_f) {
-      issue_stage(a, fc, lane_pool, ring_dst + fslot * kSlotBytes, stride, max_row, known);
+      issue_stage(a, epoch, fc, lane_pool, ring_dst + fslot * kSlotBytes, stride, max_row, known);
       have_f = walk_next(sp, fc);
     }
     cp_async_commit();
@@ -513,8 +503,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       }
       continue;
     }
-    // split segment: record (m, l, O) in slot 0 (the share's first segment) or 1
+    // split segment: record (m, l, O) in slot 0 (the share's first segment)
+    // or 1; the block merges the records of its warps once they are all done
     const int rslot = seg0 <= share_begin ? 0 : 1;
+    const int W0 = blockIdx.x * WARPS;
+    if (lane == 0 && W == max(w_first, W0)) {
+      // the first of this block's warps holding a record lists the segment
+      const int ba = w_first / WARPS, bb = w_last / WARPS;
+      const int slot_here = seg0 <= sp.begin(W0) ? 0 : 1;
+      const int slot_ba = ba == (int)blockIdx.x ? slot_here : (seg0 <= sp.begin(ba * WARPS) ? 0 : 1);
+      const int t = atomicAdd(&bt.n, 1);
+      bt.task[t] = SegTask{cc.s_req, cc.s_head, W, min(w_last, W0 + WARPS - 1), ba, bb, rslot, slot_ba, slot_here};
+    }
     float* rec = a.part + ((int64_t)W * 2 + rslot) * kPartFloats;
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
@@ -531,87 +531,228 @@ __global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) 
       ml[(2 * tig + 1) * 2] = m_b;
       ml[(2 * tig + 1) * 2 + 1] = lb;
     }
-    __threadfence();
-    __syncwarp();
-    const int seg_id = cc.s_req * kKV + cc.s_head;
-    int old = 0;
-    if (lane == 0) old = atomicAdd(&a.seg_count[seg_id], 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != w_last - w_first) continue;
+  }
+}
 
-    // the last warp of the segment merges the records: lane -> query head
-    // lane / 4, channels [32 (lane % 4), 32 (lane % 4) + 32), in two halves
-    __threadfence();
-    if (lane == 0) a.seg_count[seg_id] = 0;
-    const int hq = lane >> 2;
-    // record r of the segment: warp w_first + r; warp w_first holds it in
-    // record 1 unless its share starts at the segment.  The records' loads
-    // are issued in batches so that their L2 latencies overlap.
-    const int first_slot = sp.begin(w_first) != seg0 ? 1 : 0;
-    const int nrec = w_last - w_first + 1;
-    auto rec_of = [&](int r) -> const float* {
-      return a.part + ((int64_t)(w_first + r) * 2 + (r == 0 ? first_slot : 0)) * kPartFloats;
-    };
-    // one pass over the records, two at a time: every lane's 32 channels
-    // and its head's (m, l) of each are in flight together, and a running
-    // max M rescales the sums as it grows
-    constexpr int kOB = 2;
-    const int c0 = (lane & 3) * 32;
-    float M = kNegInf, S = 0.f;
-    float o[32];
+// ------------------------------------------------------------------ merging split segments
+//
+// Once every warp of a block has finished its share (one block barrier),
+// the block merges the records its warps wrote for each split segment, all
+// 256 threads at once (two segments at a time, 128 threads each: thread
+// -> query head (t % 128) / 16, channels 8 ((t % 128) % 16) .. + 8), so a
+// merge is one round of loads.  A segment whose warps all belong to this
+// block is finished here and written to the output.  One that continues
+// into other blocks becomes a block record (the same (m, l, O) form) and
+// the block arrives on the segment's counter (acq_rel atomic); the last
+// block to arrive merges the block records the same way.  Merge order is
+// fixed (records in warp / block order), so results do not depend on
+// arrival order.
+
+// Records r = 0 .. nr - 1 (rec(r) -> the record) merged for one query head
+// and 8 channels: running max M, sum S = sum_r 2^(m_r - M) l_r, O likewise.
+template <typename RecFn>
+__device__ __forceinline__ void merge_records(int nr, int h, int c, RecFn rec, float& M, float& S, float (&o)[8]) {
+  M = kNegInf;
+  S = 0.f;
 #pragma unroll
-    for (int e = 0; e < 32; ++e) o[e] = 0.f;
-    for (int r0 = 0; r0 < nrec; r0 += kOB) {
-      float2 ml[kOB];
-      float4 x[kOB][8];
+  for (int e = 0; e < 8; ++e) o[e] = 0.f;
+  for (int r0 = 0; r0 < nr; r0 += 8) {
+    float2 ml[8];
+    float4 x[8][2];
 #pragma unroll
-      for (int j = 0; j < kOB; ++j) {
-        if (r0 + j < nrec) {
-          const float* rw = rec_of(r0 + j);
-          ml[j] = __ldcg(reinterpret_cast<const float2*>(rw + kG * kD + hq * 2));
-          const float4* src = reinterpret_cast<const float4*>(rw + hq * kD + c0);
-#pragma unroll
-          for (int v = 0; v < 8; ++v) x[j][v] = __ldcg(src + v);
-        } else {
-          ml[j] = make_float2(kNegInf, 0.f);
-#pragma unroll
-          for (int v = 0; v < 8; ++v) x[j][v] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+    for (int j = 0; j < 8; ++j) {
+      if (r0 + j < nr) {
+        const float* rw = rec(r0 + j);
+        ml[j] = __ldcg(reinterpret_cast<const float2*>(rw + kG * kD + h * 2));
+        const float4* src = reinterpret_cast<const float4*>(rw + h * kD + c);
+        x[j][0] = __ldcg(src);
+        x[j][1] = __ldcg(src + 1);
+      } else {
+        ml[j] = make_float2(kNegInf, 0.f);
+        x[j][0] = x[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      float Mb = M;
-#pragma unroll
-      for (int j = 0; j < kOB; ++j) Mb = fmaxf(Mb, ml[j].x);
-      if (Mb == kNegInf) continue;
-      const float sc = fast_exp2(M - Mb);  // 0 while M is -inf (S and o are 0 then)
-      S *= sc;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) o[e] *= sc;
-#pragma unroll
-      for (int j = 0; j < kOB; ++j) {
-        const float f = ml[j].x == kNegInf ? 0.f : fast_exp2(ml[j].x - Mb);
-        S += f * ml[j].y;
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          o[4 * v] += f * x[j][v].x;
-          o[4 * v + 1] += f * x[j][v].y;
-          o[4 * v + 2] += f * x[j][v].z;
-          o[4 * v + 3] += f * x[j][v].w;
-        }
-      }
-      M = Mb;
     }
-    const float inv = 1.f / S;
-    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)cc.s_req * a.out_stride +
-                         (cc.s_head * kG + hq) * kD + c0;
+    float Mb = M;
 #pragma unroll
-    for (int e = 0; e < 32; e += 2) {
-      __nv_bfloat162 pr;
-      pr.x = __float2bfloat16_rn(o[e] * inv);
-      pr.y = __float2bfloat16_rn(o[e + 1] * inv);
-      *reinterpret_cast<__nv_bfloat162*>(out + e) = pr;
+    for (int j = 0; j < 8; ++j) Mb = fmaxf(Mb, ml[j].x);
+    if (Mb == kNegInf) continue;
+    const float sc = fast_exp2(M - Mb);  // 0 while M is -inf (S and o are 0 then)
+    S *= sc;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] *= sc;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float f = ml[j].x == kNegInf ? 0.f : fast_exp2(ml[j].x - Mb);
+      S += f * ml[j].y;
+      o[0] += f * x[j][0].x;
+      o[1] += f * x[j][0].y;
+      o[2] += f * x[j][0].z;
+      o[3] += f * x[j][0].w;
+      o[4] += f * x[j][1].x;
+      o[5] += f * x[j][1].y;
+      o[6] += f * x[j][1].z;
+      o[7] += f * x[j][1].w;
+    }
+    M = Mb;
+  }
+}
+
+// Final output of (request, KV head) = (req, head): O / S in bf16.
+__device__ __forceinline__ void store_output(const AttnArgs& a, int req, int head, int h, int c, float S,
+                                             const float (&o)[8]) {
+  const float inv = 1.f / S;
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)req * a.out_stride + (head * kG + h) * kD + c;
+  uint4 v;
+  __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
+  __nv_bfloat162 p1 = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
+  __nv_bfloat162 p2 = __floats2bfloat162_rn(o[4] * inv, o[5] * inv);
+  __nv_bfloat162 p3 = __floats2bfloat162_rn(o[6] * inv, o[7] * inv);
+  v.x = bf162_bits(p0);
+  v.y = bf162_bits(p1);
+  v.z = bf162_bits(p2);
+  v.w = bf162_bits(p3);
+  if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+    *reinterpret_cast<uint4*>(out) = v;
+  } else {  // the output row stride keeps 4-byte alignment only
+    uint32_t* o32 = reinterpret_cast<uint32_t*>(out);
+    o32[0] = v.x;
+    o32[1] = v.y;
+    o32[2] = v.z;
+    o32[3] = v.w;
+  }
+}
+
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+template <int WARPS>
+__device__ void merge_block(const AttnArgs& a, const BlockTasks& bt) {
+  static_assert(WARPS == kAttnWarpsPerSm, "two segments at a time, 128 threads x 8 channels each");
+  __shared__ int s_last[2];
+  const int tid = threadIdx.x;
+  const int ntask = bt.n;
+  const int half = tid >> 7, t7 = tid & 127;
+  const int h = t7 >> 4, c = (t7 & 15) * 8;
+  for (int t0 = 0; t0 < ntask; t0 += 2) {
+    const int ti = t0 + half;
+    const bool mine = ti < ntask;
+    SegTask tk{};
+    float M = kNegInf, S = 0.f, o[8];
+    if (mine) {
+      tk = bt.task[ti];
+      // record of warp w for this segment: slot 0 when it is the warp's first segment
+      merge_records(tk.wb - tk.wa + 1, h, c,
+                    [&](int r) {
+                      return a.part + ((int64_t)(tk.wa + r) * 2 + (r == 0 ? tk.slot_wa : 0)) * kPartFloats;
+                    },
+                    M, S, o);
+      if (tk.ba == tk.bb) {
+        store_output(a, tk.req, tk.head, h, c, S, o);
+      } else {
+        // the block record: slot 0 when the segment starts at or before this block's range
+        float* rec = a.bpart + ((int64_t)blockIdx.x * 2 + tk.slot_here) * kPartFloats;
+        float4* dst = reinterpret_cast<float4*>(rec + h * kD + c);
+        dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+        if ((t7 & 15) == 0) *reinterpret_cast<float2*>(rec + kG * kD + h * 2) = make_float2(M, S);
+      }
+    }
+    __syncthreads();  // the block records are written
+    if (mine && t7 == 0 && tk.ba != tk.bb) {
+      const int seg_id = tk.req * kKV + tk.head;
+      const bool last = atom_add_acq_rel_gpu(&a.seg_count[seg_id], 1) == tk.bb - tk.ba;
+      if (last) a.seg_count[seg_id] = 0;  // ready for the next launch
+      s_last[half] = last;
+    }
+    __syncthreads();
+    if (mine && tk.ba != tk.bb && s_last[half]) {
+      merge_records(tk.bb - tk.ba + 1, h, c,
+                    [&](int r) {
+                      return a.bpart + ((int64_t)(tk.ba + r) * 2 + (r == 0 ? tk.slot_ba : 0)) * kPartFloats;
+                    },
+                    M, S, o);
+      store_output(a, tk.req, tk.head, h, c, S, o);
     }
   }
+}
+
+// Every block read the call's epoch at its start; the last of the grid's
+// blocks to exit (idle ones included) advances the call counter for the next call.
+__device__ __forceinline__ void exit_arrival(const AttnArgs& a, uint32_t epoch) {
+  if (a.call_counter == nullptr) return;  // a caller-given epoch
+  if (atom_add_acq_rel_gpu(a.exit_count, 1) == (int)gridDim.x - 1) {
+    *a.exit_count = 0;
+    *a.call_counter = next_call_counter(epoch - 1);
+  }
+}
+
+template <int WARPS, int SLOTS>
+__global__ void __launch_bounds__(WARPS * 32, 1) attn_stream_kernel(AttnArgs a) {
+  using Cfg = StreamCfg<WARPS, SLOTS>;
+  // behind a fused selection the ready words order the reads instead of the
+  // grid dependency; the selection's own wait keeps earlier grids ahead
+  if (a.ready == nullptr) wait_prior_grid();
+  allow_next_grid();
+  extern __shared__ __align__(128) char smem[];
+  __shared__ BlockTasks s_tasks;
+  __shared__ uint32_t s_epoch;
+  int32_t* s_prefix4 = reinterpret_cast<int32_t*>(smem + Cfg::kRing);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  char* ring = smem + (size_t)warp * SLOTS * kSlotBytes;
+  if (threadIdx.x == 0) s_tasks.n = 0;
+  // this call's epoch (the selection read the same counter value), by a
+  // thread outside warp 0, whose prefix loads come first
+  if (threadIdx.x == 32)
+    s_epoch = a.ready == nullptr ? 0u : a.call_counter != nullptr ? ld_volatile_u32(a.call_counter) + 1 : a.fixed_epoch;
+
+  // segment prefix 4 * P_i over the batch (warp 0, 32 requests at a time)
+  if (warp == 0) {
+    int32_t run = 0;
+    for (int b0 = 0; b0 < a.bs; b0 += 32) {
+      const int b = b0 + lane;
+      int32_t n = 0;
+      if (b < a.bs) {
+        const int64_t L = a.seq_lens[b];
+        n = (int32_t)(L < a.top_k ? (L < 0 ? 0 : L) : a.top_k);
+      }
+      int32_t incl = 4 * n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (b < a.bs) s_prefix4[b + 1] = run + incl;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) s_prefix4[0] = 0;
+  }
+  __syncthreads();
+
+  Split sp;
+  sp.prefix4 = s_prefix4;
+  sp.bs = a.bs;
+  sp.T = s_prefix4[a.bs];
+  const uint32_t epoch = s_epoch;
+  if (sp.T == 0) {
+    if (a.ready != nullptr && threadIdx.x == 0) exit_arrival(a, epoch);
+    return;
+  }
+  const int grid_warps = gridDim.x * WARPS;
+  sp.NW = min(grid_warps, max(1, sp.T / kMinShare));
+  const int W = blockIdx.x * WARPS + warp;
+  if (blockIdx.x * WARPS >= sp.NW) {
+    // the whole block is idle; it still counts as exited
+    if (a.ready != nullptr && threadIdx.x == 0) exit_arrival(a, epoch);
+    return;
+  }
+  if (W < sp.NW) stream_share<WARPS, SLOTS>(a, epoch, sp, W, ring, s_tasks);
   cp_async_wait<0>();
+  __syncthreads();  // every warp's records are written and its segments listed
+  merge_block<WARPS>(a, s_tasks);
+  if (a.ready != nullptr && threadIdx.x == 0) exit_arrival(a, epoch);
 }
 
 // ------------------------------------------------------------------ generic path
@@ -675,17 +816,7 @@ __global__ void attn_generic_kernel(AttnArgs a, int q_heads, int kv_heads, int D
   }
 }
 
-int g_sm_count = 0;
-
-int sm_count() {
-  if (g_sm_count == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
-    if (g_sm_count <= 0) g_sm_count = 148;
-  }
-  return g_sm_count;
-}
+int sm_count() { return device_sm_count(); }
 
 }  // namespace
 }  // namespace qq
@@ -697,13 +828,9 @@ template <int WARPS, int SLOTS>
 int launch_stream_variant(const AttnArgs& a, cudaStream_t s) {
   static_assert(WARPS <= kAttnWarpsPerSm, "the workspace holds partial records for kAttnWarpsPerSm warps per SM");
   using Cfg = StreamCfg<WARPS, SLOTS>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(attn_stream_kernel<WARPS, SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)Cfg::kSmem) != cudaSuccess)
-      return QQ_ERR_CUDA;
-    attr_set = true;
-  }
+  static SmemLimit limit;  // per device
+  const int rc = limit.ensure((const void*)attn_stream_kernel<WARPS, SLOTS>, Cfg::kSmem);
+  if (rc != QQ_OK) return rc;
   return launch_pdl(attn_stream_kernel<WARPS, SLOTS>, dim3(sm_count()), dim3(Cfg::kThreads), Cfg::kSmem, s, a);
 }
 
@@ -723,13 +850,26 @@ extern "C" size_t qq_workspace_bytes(int max_bs, int top_k, int q_heads, int hea
 
 namespace qq {
 
+// The geometry and alignment the streaming kernel handles (else the generic kernel runs).
+bool stream_fast_path(int bs, int top_k, int dtype, int q_heads, int kv_heads, int head_dim, int64_t q_stride,
+                      const int32_t* rows, const void* k_pool, const void* v_pool, int64_t kv_row_stride,
+                      const void* out, int64_t out_stride) {
+  const int esz = dtype == QQ_BF16 ? 2 : 4;
+  return dtype == QQ_BF16 && kv_heads == kKV && head_dim == kD && q_heads == kH &&
+         (kv_row_stride * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(k_pool) % 16) == 0 &&
+         (reinterpret_cast<uintptr_t>(v_pool) % 16) == 0 && (q_stride % 2) == 0 && (out_stride % 2) == 0 &&
+         (reinterpret_cast<uintptr_t>(out) % 4) == 0 && (int64_t)bs * top_k * kKV < (1ll << 31) &&
+         top_k % kToks == 0 && (reinterpret_cast<uintptr_t>(rows) % 16) == 0 && kv_row_stride * esz < (1ll << 32);
+}
+
 // qq_sparse_decode_attention; with `ready` the streaming kernel reads a
-// request's rows once ready[i] == epoch (see ensure_ready).
+// request's rows once ready[i] holds the call's epoch (see ensure_ready).
 int sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, int dtype, int q_heads,
                             int kv_heads, int head_dim, int64_t q_stride, const int32_t* rows,
                             const void* k_pool, const void* v_pool, int64_t kv_row_stride, int64_t num_rows,
                             float scaling, void* out, int64_t out_stride, uint32_t* err, void* workspace,
-                            size_t workspace_bytes, void* stream, const uint32_t* ready, uint32_t epoch) {
+                            size_t workspace_bytes, void* stream, const uint32_t* ready, uint32_t* call_counter,
+                            uint32_t fixed_epoch = 0, uint64_t wait_limit_ns = kWaitLimitNs) {
   if (batch == nullptr || q == nullptr || rows == nullptr || k_pool == nullptr || v_pool == nullptr ||
       out == nullptr || top_k <= 0 || kv_heads <= 0 || head_dim <= 0 || q_heads % kv_heads != 0 ||
       num_rows <= 0)
@@ -757,35 +897,31 @@ int sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, int
   a.out_stride = out_stride;
   a.err = err;
   a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kPartialOffset);
+  a.bpart = a.part + attn_warp_partial_floats(sm_count());
   a.seg_count = ws_counters(workspace, kCounterAttn);
   cudaStream_t s = as_stream(stream);
 
-  const bool fast = dtype == QQ_BF16 && kv_heads == kKV && head_dim == kD && q_heads == kH &&
-                    (kv_row_stride * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(k_pool) % 16) == 0 &&
-                    (reinterpret_cast<uintptr_t>(v_pool) % 16) == 0 && (q_stride % 2) == 0 &&
-                    (out_stride % 2) == 0 && (reinterpret_cast<uintptr_t>(out) % 4) == 0 &&
-                    (int64_t)batch->bs * top_k * kKV < (1ll << 31) && top_k % kToks == 0 &&
-                    (reinterpret_cast<uintptr_t>(rows) % 16) == 0 && kv_row_stride * esz < (1ll << 32);
-  if (fast) {
+  if (stream_fast_path(batch->bs, top_k, dtype, q_heads, kv_heads, head_dim, q_stride, rows, k_pool, v_pool,
+                       kv_row_stride, out, out_stride)) {
     a.ready = ready;
-    a.epoch = epoch;
+    a.call_counter = call_counter;
+    a.exit_count = call_counter != nullptr ? reinterpret_cast<int32_t*>(call_counter + 1) : nullptr;
+    a.fixed_epoch = fixed_epoch;
+    a.wait_limit_ns = wait_limit_ns;
     return launch_stream(a, s);
   }
   const int G = q_heads / kv_heads;
   const size_t smem = sizeof(float) * ((size_t)G * head_dim + (size_t)G * top_k + 2 * (size_t)G);
   if (smem > 200 * 1024) return QQ_ERR_UNSUPPORTED;
   dim3 grid(batch->bs, kv_heads);
+  static SmemLimit limit_bf16, limit_f32;  // per device
   if (dtype == QQ_BF16) {
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(attn_generic_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return QQ_ERR_CUDA;
+    const int rc = limit_bf16.ensure((const void*)attn_generic_kernel<__nv_bfloat16>, smem);
+    if (rc != QQ_OK) return rc;
     attn_generic_kernel<__nv_bfloat16><<<grid, 128, smem, s>>>(a, q_heads, kv_heads, head_dim);
   } else {
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(attn_generic_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
-      return QQ_ERR_CUDA;
+    const int rc = limit_f32.ensure((const void*)attn_generic_kernel<float>, smem);
+    if (rc != QQ_OK) return rc;
     attn_generic_kernel<float><<<grid, 128, smem, s>>>(a, q_heads, kv_heads, head_dim);
   }
   return launch_status();
@@ -794,11 +930,8 @@ int sparse_decode_attention(const qq_batch* batch, int top_k, const void* q, int
 int retrieve_topk(const qq_quest_state* st, int layer, const qq_batch* batch, const void* q, int q_dtype,
                   int q_heads, int64_t q_stride, int32_t* positions, int32_t* actual_lens, float* scores,
                   const qq_token_table* translate, int32_t* rows, const qq_new_token* nt, void* workspace,
-                  size_t workspace_bytes, void* stream, uint32_t* ready, uint32_t epoch);
-
-namespace {
-std::atomic<uint32_t> g_epoch{0};
-}  // namespace
+                  size_t workspace_bytes, void* stream, uint32_t* ready, const uint32_t* call_counter,
+                  uint32_t* err);
 
 }  // namespace qq
 
@@ -810,7 +943,21 @@ extern "C" int qq_sparse_decode_attention(const qq_batch* batch, int top_k, cons
                                           size_t workspace_bytes, void* stream) {
   return qq::sparse_decode_attention(batch, top_k, q, dtype, q_heads, kv_heads, head_dim, q_stride, rows, k_pool,
                                      v_pool, kv_row_stride, num_rows, scaling, out, out_stride, err, workspace,
-                                     workspace_bytes, stream, nullptr, 0);
+                                     workspace_bytes, stream, nullptr, nullptr);
+}
+
+extern "C" int qq_sparse_decode_attention_ready(const qq_batch* batch, int top_k, const void* q, int dtype,
+                                                int q_heads, int kv_heads, int head_dim, int64_t q_stride,
+                                                const int32_t* rows, const void* k_pool, const void* v_pool,
+                                                int64_t kv_row_stride, int64_t num_rows, float scaling, void* out,
+                                                int64_t out_stride, uint32_t* err, const uint32_t* ready,
+                                                uint32_t epoch, uint64_t wait_limit_ns, void* workspace,
+                                                size_t workspace_bytes, void* stream) {
+  if (ready == nullptr || epoch == 0) return QQ_ERR_INVALID;
+  return qq::sparse_decode_attention(batch, top_k, q, dtype, q_heads, kv_heads, head_dim, q_stride, rows, k_pool,
+                                     v_pool, kv_row_stride, num_rows, scaling, out, out_stride, err, workspace,
+                                     workspace_bytes, stream, ready, nullptr, epoch,
+                                     wait_limit_ns == 0 ? kWaitLimitNs : wait_limit_ns);
 }
 
 extern "C" int qq_quest_decode_attention(const qq_quest_state* st, int layer, const qq_batch* batch,
@@ -824,15 +971,24 @@ extern "C" int qq_quest_decode_attention(const qq_quest_state* st, int layer, co
   if (st == nullptr || batch == nullptr || rows == nullptr || translate == nullptr) return QQ_ERR_INVALID;
   if (workspace == nullptr || workspace_bytes < qq_workspace_bytes(batch->bs, st->top_k, q_heads, st->head_dim))
     return QQ_ERR_WORKSPACE;
-  uint32_t epoch = ++g_epoch;
-  if (epoch == 0) epoch = ++g_epoch;  // 0 is a cleared word
-  uint32_t* ready = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + ready_offset(sm_count()));
+  // ready words only when the streaming kernel follows (the generic one is stream-ordered)
+  const bool early = stream_fast_path(batch->bs, st->top_k, q_dtype, q_heads, st->kv_heads, st->head_dim, q_stride,
+                                      rows, k_pool, v_pool, kv_row_stride, out, out_stride);
+  char* ws = static_cast<char*>(workspace);
+  uint32_t* ready = early ? reinterpret_cast<uint32_t*>(ws + ready_offset(sm_count())) : nullptr;
+  uint32_t* counter = early ? reinterpret_cast<uint32_t*>(ws + epoch_offset(sm_count())) : nullptr;
   int rc = retrieve_topk(st, layer, batch, q, q_dtype, q_heads, q_stride, positions, actual_lens, scores,
-                         translate, rows, new_token, workspace, workspace_bytes, stream, ready, epoch);
+                         translate, rows, new_token, workspace, workspace_bytes, stream, ready, counter, err);
   if (rc != QQ_OK) return rc;
-  return sparse_decode_attention(batch, st->top_k, q, q_dtype, q_heads, st->kv_heads, st->head_dim, q_stride,
-                                 rows, k_pool, v_pool, kv_row_stride, num_rows, scaling, out, out_stride, err,
-                                 workspace, workspace_bytes, stream, ready, epoch);
+  rc = sparse_decode_attention(batch, st->top_k, q, q_dtype, q_heads, st->kv_heads, st->head_dim, q_stride, rows,
+                               k_pool, v_pool, kv_row_stride, num_rows, scaling, out, out_stride, err, workspace,
+                               workspace_bytes, stream, ready, counter);
+  if (rc != QQ_OK && early) {
+    // the selection published this call's epoch but no attention will
+    // advance the counter: clear the words so the next call cannot match them
+    cudaMemsetAsync(ready, 0, sizeof(uint32_t) * QQ_MAX_BS, as_stream(stream));
+  }
+  return rc;
 }
 
 // ------------------------------------------------------------------ attention without a workspace
@@ -868,12 +1024,13 @@ constexpr int kNoAllocBlocks = 148;
 constexpr int kNoAllocWarps = 8;  // warps per block of the instantiation below
 constexpr int kNoAllocSlots = 3;
 constexpr size_t kNoAllocCounterBytes = sizeof(int32_t) * kKV * QQ_NOALLOC_MAX_BS;
-constexpr size_t kNoAllocPartialBytes =
-    sizeof(float) * (size_t)kNoAllocBlocks * kNoAllocWarps * 2 * kPartFloats;
+constexpr size_t kNoAllocWarpPartialBytes = sizeof(float) * (size_t)kNoAllocBlocks * kNoAllocWarps * 2 * kPartFloats;
+constexpr size_t kNoAllocPartialBytes = kNoAllocWarpPartialBytes + sizeof(float) * (size_t)kNoAllocBlocks * 2 * kPartFloats;
 constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + kNoAllocPartialBytes;
 static_assert(kNoAllocCounterBytes % 256 == 0, "partials start 256-byte aligned");
+static_assert(kNoAllocScratchBytes == 11098624, "the size the header documents");
 
-// 16 KiB of counters + 9.4 MiB of partial records (9,867,264 bytes).
+// 16 KiB of counters + 10.6 MiB of partial records, per warp and per block (11,098,624 bytes).
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
@@ -950,6 +1107,7 @@ extern "C" int qq_sparse_decode_attention_noalloc(const qq_batch* batch, int top
   a.err = err;
   a.seg_count = static_cast<int32_t*>(scratch);
   a.part = reinterpret_cast<float*>(static_cast<char*>(scratch) + kNoAllocCounterBytes);
+  a.bpart = reinterpret_cast<float*>(static_cast<char*>(scratch) + kNoAllocCounterBytes + kNoAllocWarpPartialBytes);
   using Cfg = StreamCfg<kNoAllocWarps, kNoAllocSlots>;
   const int blocks = sm_count() < kNoAllocBlocks ? sm_count() : kNoAllocBlocks;
   attn_stream_kernel<kNoAllocWarps, kNoAllocSlots><<<blocks, Cfg::kThreads, Cfg::kSmem, s>>>(a);

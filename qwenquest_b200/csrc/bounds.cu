@@ -125,6 +125,7 @@ struct StepArgs {
   const int64_t* rows;
   const int32_t* r2t;
   int64_t r2t_stride;
+  int64_t r2t_rows;  // 0: not checked
   int64_t buf;
   int32_t* counters;
 };
@@ -141,6 +142,8 @@ __global__ void decode_step_kernel(StepArgs a) {
   const int g = blockIdx.y;
   const qq_quest_state& st = a.st;
   const int64_t req = a.reqs[i];
+  // a request index outside the state (or the table) is skipped: nothing of it is read or written
+  if (req < 0 || req >= st.max_reqs || (a.r2t != nullptr && a.r2t_rows > 0 && req >= a.r2t_rows)) return;
   const int P = st.page_size;
   const bool skip = a.skip != nullptr && a.skip[req] != 0;
   const int count = st.running_token_count[req];
@@ -307,6 +310,7 @@ extern "C" int qq_quest_decode_step(const qq_quest_state* st, int flags, int lay
   a.rows = rows;
   a.r2t = table ? table->req_to_token : nullptr;
   a.r2t_stride = table ? table->stride : 0;
+  a.r2t_rows = table ? table->rows : 0;
   a.buf = device_buffer_size;
   a.counters = ws_counters(workspace, kCounterStep);
   dim3 grid(batch->bs, a.groups);

@@ -1,7 +1,9 @@
 // Shared device helpers for the Quest kernels (sm_100a).
 #pragma once
 
+#include <atomic>
 #include <cstdlib>
+#include <mutex>
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -145,6 +147,60 @@ inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) == cudaSuccess ? QQ_OK : QQ_ERR_CUDA;
 }
 
+// ---------------------------------------------------------------- per-device state
+//
+// Values and kernel attributes are per device: a process may drive several
+// GPUs, from several host threads.
+
+constexpr int kMaxDevices = 64;
+
+inline int current_device() {
+  int d = -1;
+  return cudaGetDevice(&d) == cudaSuccess ? d : -1;
+}
+
+// The current device's SM count, queried once per device.
+inline int device_sm_count() {
+  static std::atomic<int> cache[kMaxDevices];
+  const int d = current_device();
+  const bool cached = d >= 0 && d < kMaxDevices;
+  if (cached) {
+    const int v = cache[d].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d < 0 ? 0 : d) != cudaSuccess || n <= 0) n = 148;
+  if (cached) cache[d].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+// A kernel's dynamic shared-memory limit on the current device, raised (never
+// lowered) to what a launch needs, once per size and device, under a lock.
+class SmemLimit {
+ public:
+  int ensure(const void* kernel, size_t bytes) {
+    const int need = (int)bytes;
+    if (need <= 48 * 1024) return QQ_OK;  // within the default limit
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return set(kernel, need);
+    if (limit_[d].load(std::memory_order_acquire) >= need) return QQ_OK;
+    std::lock_guard<std::mutex> lock(mutex_);
+    if (limit_[d].load(std::memory_order_relaxed) >= need) return QQ_OK;
+    const int rc = set(kernel, need);
+    if (rc == QQ_OK) limit_[d].store(need, std::memory_order_release);
+    return rc;
+  }
+
+ private:
+  static int set(const void* kernel, int bytes) {
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess
+               ? QQ_OK
+               : QQ_ERR_CUDA;
+  }
+  std::atomic<int> limit_[kMaxDevices] = {};
+  std::mutex mutex_;
+};
+
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? QQ_OK : QQ_ERR_CUDA;
@@ -169,16 +225,33 @@ inline uint64_t* ws_select_lists(void* ws) {
 constexpr size_t kPartialOffset = kSelectListOffset + kSelectListBytes;
 
 // Attention partials: two (m, l, O) records of 8 query heads x 128 channels
-// per warp of the streaming grid (8 warps per SM).
+// per warp of the streaming grid (8 warps per SM), then two per block.
 constexpr int kAttnWarpsPerSm = 8;  // warps per block of the streaming kernel
 constexpr size_t kAttnPartialFloats = 2 * (8 * 128 + 2 * 8);
-inline size_t attn_partial_floats(int sm_count) {
+inline size_t attn_warp_partial_floats(int sm_count) {
   return (size_t)sm_count * kAttnWarpsPerSm * kAttnPartialFloats;
+}
+inline size_t attn_partial_floats(int sm_count) {
+  return attn_warp_partial_floats(sm_count) + (size_t)sm_count * kAttnPartialFloats;
 }
 // Then one ready word per request (uint32) for the fused selection +
 // attention call: the selection stores the call's epoch once the request's
-// rows are written, the attention spins on it.
+// rows are written, the attention spins on it.  Then the epoch state: the
+// call counter (the current call's epoch is counter + 1, never 0) and the
+// attention blocks' exit counter; the attention's last block to exit
+// advances the call counter, so epochs live on the device and a captured
+// call renews them on every replay.
 inline size_t ready_offset(int sm_count) { return kPartialOffset + sizeof(float) * attn_partial_floats(sm_count); }
-inline size_t workspace_end(int sm_count) { return ready_offset(sm_count) + sizeof(uint32_t) * QQ_MAX_BS; }
+inline size_t epoch_offset(int sm_count) { return ready_offset(sm_count) + sizeof(uint32_t) * QQ_MAX_BS; }
+inline size_t workspace_end(int sm_count) { return epoch_offset(sm_count) + 2 * sizeof(uint32_t); }
+
+// The epoch that follows counter value c (0 and 0xFFFFFFFF are never epochs: ready words start at 0).
+__host__ __device__ __forceinline__ uint32_t next_call_counter(uint32_t c) { return c + 2 == 0 ? 0u : c + 1; }
+
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 }  // namespace qq

@@ -34,16 +34,7 @@ constexpr int kExtendMaxWordsPerBlock = 64;
 constexpr int kExtendMinWordsPerBlock = 16;
 constexpr int kExtendBlocksPerSm = 4;
 
-int extend_sm_count() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
+int extend_sm_count() { return device_sm_count(); }
 
 struct ExtendArgs {
   qq_quest_state st;
@@ -59,6 +50,7 @@ struct ExtendArgs {
   int64_t num_tokens;
   const int32_t* r2t;
   int64_t r2t_stride;
+  int64_t r2t_rows;  // 0: not checked
   const char* k_src;
   const char* v_src;
   int64_t src_stride;  // bytes between new tokens
@@ -147,6 +139,11 @@ __global__ void __launch_bounds__(kExtendThreads, kExtendBlocksPerSm) extend_kv_
   const int64_t req = a.reqs[i];
   const int64_t off = a.offsets[i];
   const int64_t p0 = (int64_t)page * P;
+  // a request index outside the table (or the Quest state) is reported once and its request skipped
+  if (req < 0 || (a.r2t_rows > 0 && req >= a.r2t_rows) || (a.bounds && req >= a.st.max_reqs)) {
+    if (page == 0 && blockIdx.z == 0 && threadIdx.x == 0) raise_error(a.err, QQ_DEV_ERR_BOUNDS);
+    return;
+  }
   if (p0 >= seq) return;
   const int64_t p1 = seq < p0 + P ? seq : p0 + P;
   const bool hot_page = a.hot_k != nullptr && p0 < a.hot_buf;
@@ -362,6 +359,7 @@ extern "C" int qq_quest_extend_kv(const qq_quest_state* st, int layer, int write
   a.num_tokens = eb->num_tokens;
   a.r2t = table->req_to_token;
   a.r2t_stride = table->stride;
+  a.r2t_rows = table->rows;
   a.k_src = static_cast<const char*>(k);
   a.v_src = static_cast<const char*>(v);
   a.src_stride = src_stride * esize;

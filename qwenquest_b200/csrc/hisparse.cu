@@ -391,9 +391,9 @@ extern "C" int qq_hisparse_swap_in(const qq_hisparse_state* hs, int layer, const
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (smem > (size_t)max_optin) return QQ_ERR_UNSUPPORTED;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(swap_in_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return QQ_ERR_CUDA;
+  static SmemLimit limit;  // per device
+  const int rc = limit.ensure((const void*)swap_in_kernel, smem);
+  if (rc != QQ_OK) return rc;
   swap_in_kernel<<<batch->bs, kSwapThreads, smem, as_stream(stream)>>>(a);
   return launch_status();
 }

@@ -43,7 +43,9 @@ struct SelectArgs {
   float* scores;
   const int32_t* r2t;
   int64_t r2t_stride;
+  int64_t r2t_rows;  // 0: not checked
   int32_t* rows;
+  uint32_t* err;     // optional: QQ_DEV_ERR_BOUNDS for a request index outside the state / table
   // fused new-token K/V write
   const uint32_t* nt_k;
   const uint32_t* nt_v;
@@ -63,16 +65,16 @@ struct SelectArgs {
   int score_all;  // page_scores API: score pages [0, num_pages) of every request, no selection
   int num_pages;
   uint32_t* ready;  // optional: ready[i] = epoch once request i's positions and rows are written
-  uint32_t epoch;
+  const uint32_t* call_counter;  // with ready: this call's epoch is *call_counter + 1
 };
 
 // Request i's layout is written (by the whole block, before a barrier): its
 // ready word takes this launch's epoch, after a fence, for a consumer that
 // spins on it instead of waiting for the whole grid.
-__device__ __forceinline__ void publish_ready(const SelectArgs& a, int i) {
+__device__ __forceinline__ void publish_ready(const SelectArgs& a, int i, uint32_t epoch) {
   if (a.ready == nullptr) return;
   __threadfence();
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.ready + i), "r"(a.epoch) : "memory");
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.ready + i), "r"(epoch) : "memory");
 }
 
 // Dynamic shared memory of the selection: order keys of the candidate
@@ -295,6 +297,10 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
   extern __shared__ __align__(16) unsigned char s_dyn[];  // the radix selection's keys and pages
 
   wait_prior_grid();
+  // the call's epoch (thread 0 publishes): the counter is advanced only by
+  // the previous call's attention (complete by now) and read by this call's
+  // attention; the value is used only once a request is ready
+  const uint32_t epoch = a.ready != nullptr && threadIdx.x == 0 ? ld_volatile_u32(a.call_counter) + 1 : 0u;
   allow_next_grid();
   const qq_quest_state& st = a.st;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -309,8 +315,14 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
 
   for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
     const int i = u / a.parts, j = u - (u / a.parts) * a.parts;
-    // request row, length and the query rows all in flight at once
-    const int64_t req = a.reqs[i];
+    // request row, length and the query rows all in flight at once; a
+    // request index outside the state (or the table) is reported and read
+    // as slot 0, so every address stays inside its buffer
+    const int64_t req_in = a.reqs[i];
+    const bool req_bad = req_in < 0 || req_in >= st.max_reqs ||
+                         (a.r2t != nullptr && a.r2t_rows > 0 && req_in >= a.r2t_rows);
+    const int64_t req = req_bad ? 0 : req_in;
+    if (req_bad && tid == 0 && j == 0) raise_error(a.err, QQ_DEV_ERR_BOUNDS);
     const int64_t L = a.score_all ? 0 : a.seq_lens[i];
     const QT* q = static_cast<const QT*>(a.q) + (int64_t)i * a.q_stride;
     // the new token's K/V words (part 0 writes them to the pool row below):
@@ -509,17 +521,21 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
 
     const int sel = is_long ? (int)min((int64_t)sel_req, C) : 0;
     if (lists) {
-      // the part's top 32: a merge tree over the warps' lists
-      s_lists[0][warp][lane] = top;
-      __syncthreads();
-      int cur = 0;
-      for (int n = kWarps; n > 1; n >>= 1) {
-        if (warp < n / 2)
-          s_lists[cur ^ 1][warp][lane] = top32_merge(s_lists[cur][2 * warp][lane], s_lists[cur][2 * warp + 1][lane], lane);
-        cur ^= 1;
+      // the block's top 32 of the warps' lists (a merge tree in shared memory)
+      auto block_top32 = [&](uint64_t mine) {
+        s_lists[0][warp][lane] = mine;
         __syncthreads();
-      }
-      top = s_lists[cur][0][lane];
+        int cur = 0;
+        for (int n = kWarps; n > 1; n >>= 1) {
+          if (warp < n / 2)
+            s_lists[cur ^ 1][warp][lane] =
+                top32_merge(s_lists[cur][2 * warp][lane], s_lists[cur][2 * warp + 1][lane], lane);
+          cur ^= 1;
+          __syncthreads();
+        }
+        return s_lists[cur][0][lane];
+      };
+      top = block_top32(top);
       if (a.parts > 1) {
         // the req_to_token entries of this part's top pages go to L2 while
         // the parts arrive, for the last one's translation
@@ -545,17 +561,42 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
         }
         __syncthreads();
         if (!s_last) continue;
-        if (warp == 0) {
-          top = 0;
-          for (int jj = 0; jj < a.parts; ++jj)
-            top = top32_merge(top, __ldcg(a.lists + ((size_t)i * a.parts + jj) * kSelectListLen + lane), lane);
+        const uint64_t* plist = a.lists + (size_t)i * a.parts * kSelectListLen + lane;
+        if (a.parts <= 4) {
+          // warp 0 merges its own list with the other parts' (loaded together)
+          if (warp == 0) {
+            uint64_t x[3];
+#pragma unroll
+            for (int e = 0; e < 3; ++e) {
+              const int jj = e < j ? e : e + 1;  // the other parts
+              x[e] = jj < a.parts ? __ldcg(plist + (size_t)jj * kSelectListLen) : 0ull;
+            }
+#pragma unroll
+            for (int e = 0; e < 3; ++e) top = top32_merge(top, x[e], lane);
+          }
+        } else {
+          // warp w takes lists w, w + 16, ... (four loads in flight at a
+          // time), then the merge tree joins the warps (two barriers since
+          // every warp read the first tree's result)
+          uint64_t mine = 0;
+          for (int j0 = warp; j0 < a.parts; j0 += 4 * kWarps) {
+            uint64_t x[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int jj = j0 + e * kWarps;
+              x[e] = jj < a.parts ? __ldcg(plist + (size_t)jj * kSelectListLen) : 0ull;
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) mine = top32_merge(mine, x[e], lane);
+          }
+          top = block_top32(mine);
         }
       }
       if (warp == 0 && lane < sel) s_top[lane] = (int32_t)(0xFFFFFFFFu - (uint32_t)(top & 0xFFFFFFFFu));
       __syncthreads();
       write_layout(a, i, req, L, is_long, sel, s_top);
       __syncthreads();  // s_lists and s_top are free again
-      if (tid == 0) publish_ready(a, i);
+      if (tid == 0) publish_ready(a, i, epoch);
       continue;
     }
 
@@ -574,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     __syncthreads();
     if (s_last) select_request(a, i, req, L, C, is_long, s_dyn, s_hist, s_digit, s_above, s_ngt);
     __syncthreads();  // the selection's shared memory is free again
-    if (s_last && tid == 0) publish_ready(a, i);
+    if (s_last && tid == 0) publish_ready(a, i, epoch);
   }
 }
 
@@ -621,15 +662,11 @@ inline size_t select_dyn_smem(int kw, size_t selection) {
 
 template <typename QT>
 int launch_select(const SelectArgs& a, int grid, int kw, size_t smem, cudaStream_t s) {
-  static size_t attr_smem[4] = {48 * 1024, 48 * 1024, 48 * 1024, 48 * 1024};  // the default limit
+  static SmemLimit limit[4];  // per kernel variant, per device
   const int ki = kw == 1 ? 0 : kw == 2 ? 1 : kw == 4 ? 2 : 3;
   smem = select_dyn_smem(kw, smem);
-  if (smem > attr_smem[ki]) {
-    if (cudaFuncSetAttribute(kernel_for<QT>(kw), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return QQ_ERR_CUDA;
-    attr_smem[ki] = smem;
-  }
+  const int rc = limit[ki].ensure(kernel_for<QT>(kw), smem);
+  if (rc != QQ_OK) return rc;
   switch (kw) {
     case 1: return launch_pdl(score_select_kernel<QT, 1, 4>, dim3(grid), dim3(kThreads), smem, s, a);
     case 2: return launch_pdl(score_select_kernel<QT, 2, 4>, dim3(grid), dim3(kThreads), smem, s, a);
@@ -645,16 +682,7 @@ bool valid_state(const qq_quest_state* st) {
          reinterpret_cast<uintptr_t>(st->page_bounds) % 16 == 0;
 }
 
-int g_sm_count = 0;
-int sm_count() {
-  if (g_sm_count == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
-    if (g_sm_count <= 0) g_sm_count = 148;
-  }
-  return g_sm_count;
-}
+int sm_count() { return device_sm_count(); }
 
 // Units and grid of one launch over `pages` page slots per request: with a
 // small batch every request is split into parts so that each SM streams
@@ -682,7 +710,8 @@ namespace qq {
 int retrieve_topk(const qq_quest_state* st, int layer, const qq_batch* batch, const void* q, int q_dtype,
                   int q_heads, int64_t q_stride, int32_t* positions, int32_t* actual_lens, float* scores,
                   const qq_token_table* translate, int32_t* rows, const qq_new_token* nt, void* workspace,
-                  size_t workspace_bytes, void* stream, uint32_t* ready, uint32_t epoch) {
+                  size_t workspace_bytes, void* stream, uint32_t* ready, const uint32_t* call_counter,
+                  uint32_t* err) {
   if (!valid_state(st) || batch == nullptr || layer < 0 || layer >= st->num_layers) return QQ_ERR_INVALID;
   if (st->top_k <= 0 || st->top_k % st->page_size != 0) return QQ_ERR_INVALID;
   if (batch->bs == 0) return QQ_OK;
@@ -707,11 +736,13 @@ int retrieve_topk(const qq_quest_state* st, int layer, const qq_batch* batch, co
   a.scores = scores;
   a.r2t = translate ? translate->req_to_token : nullptr;
   a.r2t_stride = translate ? translate->stride : 0;
+  a.r2t_rows = translate ? translate->rows : 0;
+  a.err = err;
   a.rows = rows;
   a.counters = ws_counters(workspace, kCounterSelect);
   a.lists = ws_select_lists(workspace);
   a.ready = ready;
-  a.epoch = epoch;
+  a.call_counter = call_counter;
   if (nt != nullptr && nt->k != nullptr) {
     const int esz = nt->dtype == QQ_F32 ? 4 : 2;
     const int64_t row_bytes = (int64_t)st->kv_heads * st->head_dim * esz;
@@ -749,7 +780,7 @@ extern "C" int qq_quest_retrieve_topk(const qq_quest_state* st, int layer, const
                                       const qq_new_token* nt, void* workspace,
                                       size_t workspace_bytes, void* stream) {
   return qq::retrieve_topk(st, layer, batch, q, q_dtype, q_heads, q_stride, positions, actual_lens, scores,
-                           translate, rows, nt, workspace, workspace_bytes, stream, nullptr, 0);
+                           translate, rows, nt, workspace, workspace_bytes, stream, nullptr, nullptr, nullptr);
 }
 
 extern "C" int qq_quest_group_queries(const void* q, int dtype, int bs, int q_heads, int kv_heads,

@@ -2,7 +2,8 @@
 
 Per decode step ``B200QuestOnlyBackend`` makes 1 + 2 x layers launches (the
 step's bounds fold, then per layer the selection and the attention) and per
-layer some Python and ctypes work to set each launch up.  Captured once in a
+layer some Python and ctypes work to set each launch up (~35 us of host time
+per layer, more than the GPU needs for a small batch).  Captured once in a
 CUDA graph, a step becomes one graph launch: the host cost of a 48-layer step
 falls from ~1.8 ms to a few tens of microseconds, and the launches keep their
 programmatic (early-launch) dependencies.
@@ -10,13 +11,16 @@ programmatic (early-launch) dependencies.
 Inputs are static: ``q``, ``k``, ``v`` (``[layers, bs, heads, head_dim]``) and
 the batch's ``req_pool_indices``, ``seq_lens`` and ``out_cache_loc`` are copied
 into buffers the graph owns before each replay; the outputs are the graph's own
-``[bs, heads * head_dim]`` tensors per layer, overwritten by the next replay.
+``[bs, heads * head_dim]`` tensors per layer, overwritten by the next replay
+(with ``stack_outputs`` also gathered into one ``[layers, bs, heads *
+head_dim]`` tensor inside the graph, for a single device-to-host copy).
 
-Inside the graph the backend makes the two calls per layer
-(``qq_quest_retrieve_topk``, then ``qq_sparse_decode_attention``): the single
-fused call tags its per-request ready words with a per-call number that a
-replay could not renew.  The HiSparse backend's step reads the batch on the
-host (its host-row free list), so it is not captured.
+Inside the graph the backend makes the same call per layer as eagerly: the
+fused ``qq_quest_decode_attention`` (selection and attention, the attention
+starting on each request as soon as its rows are written), whose per-call
+epoch is kept on the device and so is renewed on every replay; with
+``backend.fused = False`` the two calls.  The HiSparse backend's step reads
+the batch on the host (its host-row free list), so it is not captured.
 """
 
 from __future__ import annotations
@@ -37,7 +41,8 @@ class DecodeStepGraph:
     the backend's state advances only on ``replay``.
     """
 
-    def __init__(self, backend: B200QuestOnlyBackend, layers, batch: ForwardBatch, q, k, v):
+    def __init__(self, backend: B200QuestOnlyBackend, layers, batch: ForwardBatch, q, k, v, *,
+                 stack_outputs: bool = False):
         if not isinstance(backend, B200QuestOnlyBackend):
             raise TypeError("DecodeStepGraph captures B200QuestOnlyBackend decode steps")
         if backend.quest.trace is not None or backend.kernel_events is not None:
@@ -64,16 +69,12 @@ class DecodeStepGraph:
             attn_backend=backend,
         )
         self.graph = torch.cuda.CUDAGraph()
-        fused = backend.fused
-        backend.fused = False
-        try:
-            with torch.cuda.graph(self.graph):
-                backend.init_forward_metadata(self.batch)
-                self.out = [backend.forward(self.q[layer.layer_id], self.k[layer.layer_id],
-                                            self.v[layer.layer_id], layer, self.batch)
-                            for layer in self.layers]
-        finally:
-            backend.fused = fused
+        with torch.cuda.graph(self.graph):
+            backend.init_forward_metadata(self.batch)
+            self.out = [backend.forward(self.q[layer.layer_id], self.k[layer.layer_id],
+                                        self.v[layer.layer_id], layer, self.batch)
+                        for layer in self.layers]
+            self.out_stacked = torch.stack(self.out) if stack_outputs else None
 
     def replay(self, batch: ForwardBatch | None = None, q=None, k=None, v=None) -> list[torch.Tensor]:
         """Copy this step's inputs into the graph's buffers (those given), then run the step."""

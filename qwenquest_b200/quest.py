@@ -284,7 +284,7 @@ class QuestAlgorithm:
             arr, kv_dtype, k_row_stride = None, QQ_BF16, 0
         table = None
         if req_to_token is not None:
-            table = _lib.QQTokenTable(req_to_token.data_ptr(), req_to_token.stride(0))
+            table = _lib.QQTokenTable(req_to_token.data_ptr(), req_to_token.stride(0), req_to_token.shape[0])
         rc = self.lib.qq_quest_decode_step(
             self._state, flags, lb - self.start_layer, le - self.start_layer, arr, kv_dtype,
             k_row_stride or 0, batch, skip_flags.data_ptr() if skip_flags is not None else None,

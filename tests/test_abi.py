@@ -51,6 +51,12 @@ def test_argument_errors_are_reported_without_touching_a_device(lib):
     assert lib.qq_quest_init_storage(st, None) == _lib.QQ_ERR_INVALID
     assert lib.qq_quest_invalidate(None, 0, None) == _lib.QQ_ERR_INVALID
     assert lib.qq_copy_rows(None, None, 0, 0, 0, 0, None, 0, None, 0, 0, None) == _lib.QQ_ERR_INVALID
+    # the ready-word attention needs words and a nonzero epoch (0 is a cleared word)
+    b = _lib.QQBatch(0x10000, 0x10000, 1)
+    args = (b, 2048, 0x10000, _lib.QQ_BF16, 32, 4, 128, 4096, 0x10000, 0x10000, 0x10000, 512, 100, 0.1,
+            0x10000, 4096, None)
+    assert lib.qq_sparse_decode_attention_ready(*args, None, 1, 0, 0x10000, 1 << 30, None) == _lib.QQ_ERR_INVALID
+    assert lib.qq_sparse_decode_attention_ready(*args, 0x10000, 0, 0, 0x10000, 1 << 30, None) == _lib.QQ_ERR_INVALID
     with pytest.raises(ValueError):
         _lib.check(_lib.QQ_ERR_INVALID, "probe")
 

@@ -3,16 +3,21 @@
 Called through the C-ABI, it must match ``qq_sparse_decode_attention`` (the
 same attention given a workspace) within the attention tests' bf16
 tolerance, on two calls in a row: the second call reuses the library's fixed
-scratch array right after the first.  The file name sorts last, so the full
+scratch array right after the first.  Both are also checked against the CPU
+oracle's ``decode_attention`` (the reference's ``attention/ops.py:48-66``
+restated in numpy) on a sample of requests, so an error the two entry points
+shared would not pass.  The file name sorts last, so the full
 suite runs it after every other GPU test; it also passes alone in a fresh
 process, where its first call does the per-device set-up.
 """
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
+from oracle.attention import decode_attention
 from qwenquest_b200 import _lib
 from qwenquest_b200.hisparse import host_device_pointer
 
@@ -70,6 +75,15 @@ def test_noalloc_matches_the_workspace_entry_twice_in_a_row(lens, top_k):
     for out in outs:
         worst = (out.float() - ref.float()).abs().max().item()
         assert worst <= ATOL, worst
+    # the oracle, over the same rows, for requests spread over the batch
+    qn, kn, vn = (t.float().cpu().numpy() for t in (q, k, v))
+    rn, lens_n = rows.cpu().numpy(), seq.cpu().numpy()
+    for b in sorted({0, 1, bs // 3, bs // 2, bs - 2, bs - 1}):
+        r = rn[b, :min(int(lens_n[b]), top_k)].astype(np.int64)
+        want = decode_attention(qn[b], kn[r], vn[r], DIM ** -0.5, out_bf16=False)
+        for out in outs:
+            worst = float(np.abs(out[b].float().cpu().numpy() - want).max())
+            assert worst <= ATOL, (b, worst)
 
 
 def test_noalloc_rejects_what_its_fixed_scratch_cannot_hold():
