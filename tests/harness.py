@@ -251,6 +251,9 @@ class LifecycleDriver:
             out = self.backend.forward(q, k, v, layer, batch)
             out_np = out.float().cpu().numpy()
             recs = trace.records[n_before:] if trace is not None else [None] * len(running)
+            # without a trace, a B200 backend's positions are read back from its position buffer
+            pos_buf = (self.backend._positions[:len(running)].cpu().numpy()
+                       if trace is None and hasattr(self.backend, "_positions") else None)
             for i, r in enumerate(running):
                 rec = recs[i]
                 bt = lru = None
@@ -262,7 +265,8 @@ class LifecycleDriver:
                     DecodeRecord(
                         step=self._step, layer=li, req=r, slot=slots[i], seq_len=pos[i] + 1,
                         positions=(rec.positions.numpy().astype(np.int64) if rec is not None
-                                   else np.zeros(0, np.int64)),
+                                   else pos_buf[i, :min(pos[i] + 1, self.sc.top_k)].astype(np.int64)
+                                   if pos_buf is not None else np.zeros(0, np.int64)),
                         out=out_np[i], buffer_tokens=bt, lru_slots=lru,
                     )
                 )
