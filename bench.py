@@ -17,8 +17,10 @@ Every layer-step reads ~338 MB of distinct data (far beyond the 126 MB L2),
 so aliasing changes no byte counts.  Inputs are synthetic (seeded N(0,1)
 scaled per channel by LogNormal(0, 0.5)); no dataset exists for this path.
 
-``--impl reference`` times the CPU oracle (the reference algorithm restated in
-numpy) on the host cores on a bounded sample of the same workload.
+``--impl reference`` times the reference's own ``QuestOnlyBackend`` (torch on
+the host cores, CPU pools) on config 1's 64-request batch, one layer per step
+(a layer-step), with the numpy restatement under ``oracle/`` reported beside
+it; the GPU arm's ``cpu_baseline`` is the same measurement.
 
 Other single-GPU cases, each printing its own JSON line (not the headline):
 ``--case prefill`` (one 32K-token prefill's K/V write + Quest bounds over 48
@@ -634,6 +636,67 @@ def _cpu_sample(sample_reqs: int, min_seconds: float, seed: int, samples: int = 
     return out
 
 
+def reference_sample(n_req: int, steps: int, warmup: int, seed: int = 0) -> dict:
+    """The reference's own ``QuestOnlyBackend`` (``src/qwenquest/attention/quest_only.py``) on CPU pools,
+    timed on the host cores: ``n_req`` requests of config 1 (32 768-token prefixes, bounds built by its
+    own ``update_prefill_representations``), one layer; a step is ``init_forward_metadata`` +
+    ``forward`` for that layer, i.e. ``n_req / 64`` of a layer-step."""
+    from types import SimpleNamespace
+
+    from qwenquest.attention import QuestOnlyBackend
+    from qwenquest.batch import ForwardBatch, ForwardMode
+    from qwenquest.memory import MHATokenToKVPool, ReqToTokenPool
+
+    threads = host_cores()
+    torch.set_num_threads(threads)
+    total = warmup + steps
+    max_ctx = ((PREFIX + total + 1 + PAGE - 1) // PAGE) * PAGE
+    gen = torch.Generator().manual_seed(seed)
+    t0 = time.perf_counter()
+    pool = MHATokenToKVPool(n_req * max_ctx, 1, KV, D, torch.bfloat16, "cpu")
+    scale = torch.exp(0.5 * torch.randn(KV, D, generator=gen))
+    for buf in (pool.k_buffer[0], pool.v_buffer[0]):
+        for r0 in range(1, buf.shape[0], 1 << 16):  # N(0,1) x per-channel scale, in chunks
+            r1 = min(buf.shape[0], r0 + (1 << 16))
+            buf[r0:r1] = torch.randn((r1 - r0, KV, D), generator=gen).mul_(scale)
+    r2t = ReqToTokenPool(n_req, max_ctx, "cpu")
+    r2t.req_to_token.copy_((1 + torch.arange(n_req)[:, None] * max_ctx + torch.arange(max_ctx)[None]).to(torch.int32))
+    backend = QuestOnlyBackend(r2t, pool, {"algorithm": "quest", "top_k": TOP_K, "quest_page_size": PAGE})
+    for i in range(n_req):  # what the reference's _update_quest_for_extend does after a prefill
+        backend.quest.update_prefill_representations(0, i, pool.k_buffer[0], r2t.req_to_token[i, :PREFIX])
+        backend._skip_first_decode_update[i] = True
+    layer = SimpleNamespace(layer_id=0, scaling=D ** -0.5, num_heads=H, num_kv_heads=KV, head_dim=D)
+    reqs = torch.arange(n_req, dtype=torch.int64)
+    setup_s = time.perf_counter() - t0
+    times = []
+    for s in range(total):
+        pos = torch.full((n_req,), PREFIX + s, dtype=torch.int64)
+        batch = ForwardBatch(forward_mode=ForwardMode.DECODE, input_ids=torch.zeros(n_req, dtype=torch.int64),
+                             positions=pos, req_pool_indices=reqs, seq_lens=pos + 1,
+                             out_cache_loc=1 + reqs * max_ctx + pos, req_to_token_pool=r2t, token_to_kv_pool=pool,
+                             attn_backend=backend)
+        q = torch.randn((n_req, H, D), generator=gen).to(torch.bfloat16)
+        k = torch.randn((n_req, KV, D), generator=gen).mul_(scale).to(torch.bfloat16)
+        v = torch.randn((n_req, KV, D), generator=gen).mul_(scale).to(torch.bfloat16)
+        a = time.perf_counter()
+        backend.init_forward_metadata(batch)
+        backend.forward(q, k, v, layer, batch)
+        times.append(time.perf_counter() - a)
+    timed = times[warmup:]
+    sec = statistics.mean(timed)
+    return {
+        "value": (n_req / N_REQ) / sec,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "reference",
+        "sample": f"the reference's own QuestOnlyBackend (torch {torch.__version__}, CPU, {threads} threads) on "
+                  f"{n_req} of config 1's 64 requests x 1 layer, {steps} timed steps after {warmup} warm-up "
+                  f"(init_forward_metadata + forward), scaled to the 64-request layer-step",
+        "ms_per_layer_step": 1e3 * sec * N_REQ / n_req,
+        "setup_s": setup_s,
+    }
+
+
 def host_cores() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
@@ -704,6 +767,8 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-requests", type=int, default=N_REQ,
+                    help="requests of the reference's CPU sample (a layer-step of config 1 has 64)")
     ap.add_argument("--requests", type=int, default=N_REQ, help="requests per GPU (profiling cases only)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers (profiling cases only)")
     ap.add_argument("--resident", type=int, default=RESIDENT, help="physical KV buffers")
@@ -732,14 +797,10 @@ def main() -> None:
     if args.impl == "reference":
         if rank != 0:
             return
-        torch.set_num_threads(os.cpu_count() or 1)
         t0 = time.perf_counter()
-        steps = cpu_baseline(min_seconds=max(1.0, args.cpu_seconds / max(1, args.steps)),
-                             samples=args.warmup + args.steps)
-        timed = steps[args.warmup:]
-        value = statistics.mean(s["value"] for s in timed)
-        cb = dict(timed[0])
-        cb["value"] = value
+        cb = reference_sample(args.cpu_requests, args.steps, args.warmup, seed=args.seed)
+        value = cb["value"]
+        port = cpu_baseline(min_seconds=max(0.5, args.cpu_seconds / 4))[0]
         line = {
             "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * LAYERS / value,
@@ -747,8 +808,11 @@ def main() -> None:
             "dtype": "bf16",
             "data": "synthetic", "cpu_baseline": cb,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "config": {"workload": "config1: 64 req x 32768 ctx, 48 layers, Quest top_k 2048 / page 64",
+            "config": {"workload": "config1: 64 requests x 32768-token prefix, 48 layers, Quest top_k 2048 / page 64, "
+                                   "Qwen3-30B-A3B attention (32q/4kv x 128, bf16), quest mode",
                        "cpu": cpu_model(), "wall_s": time.perf_counter() - t0},
+            "port": {"value": port["value"], "sample": port["sample"], "cores": port["cores"],
+                     "what": "the numpy restatement of the same path (oracle/), for comparison"},
         }
         print(json.dumps(line))
         return
@@ -997,8 +1061,10 @@ def main() -> None:
         },
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        torch.set_num_threads(os.cpu_count() or 1)
-        line["cpu_baseline"] = cpu_baseline(min_seconds=args.cpu_seconds)[0]
+        del backend, pool, r2t, qkv, batches, hq, hk, hv, hout, ebufs
+        torch.cuda.empty_cache()
+        line["cpu_baseline"] = reference_sample(args.cpu_requests, 3, 2, seed=args.seed)
+        line["cpu_baseline_port"] = cpu_baseline(min_seconds=args.cpu_seconds)[0]
         line["config"]["cpu"] = cpu_model()
     if rank == 0:
         print(json.dumps(line))

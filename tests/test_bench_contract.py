@@ -1,10 +1,11 @@
 """The benchmark's reference arm keeps its JSON contract (CPU).
 
-``bench.py --impl reference`` times the CPU restatement of the path on the
-host cores and prints one JSON line on rank 0 with the same metric, unit and
-direction as the GPU arm, a ``cpu_baseline`` describing the sample and an
-``e2e`` object with no host<->device bytes; other ranks print nothing and
-exit 0.  It needs no GPU, so the contract is checked here with a tiny sample.
+``bench.py --impl reference`` times the reference's own ``QuestOnlyBackend``
+on the host cores and prints one JSON line on rank 0 with the same metric,
+unit and direction as the GPU arm, a ``cpu_baseline`` describing the sample
+and an ``e2e`` object with no host<->device bytes; other ranks print nothing
+and exit 0.  It needs no GPU, so the contract is checked here with a small
+sample (two of the 64 requests).
 """
 
 from __future__ import annotations
@@ -22,7 +23,7 @@ def _run(env_extra: dict) -> subprocess.CompletedProcess:
     env = dict(os.environ, **env_extra)
     return subprocess.run(
         [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "3",
-         "--cpu-seconds", "0.5"],
+         "--cpu-seconds", "0.5", "--cpu-requests", "2"],
         cwd=ROOT, env=env, capture_output=True, text=True, timeout=600,
     )
 
@@ -40,7 +41,8 @@ def test_reference_arm_prints_one_contract_line():
     assert d["value"] > 0
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["unit"] == d["unit"]
-    assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
+    assert cb["kind"] == "reference" and cb["cores"] >= 1 and "QuestOnlyBackend" in cb["sample"]
+    assert d["port"]["value"] > 0
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["config"]["workload"].startswith("config1")
 
