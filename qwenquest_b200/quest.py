@@ -17,14 +17,14 @@ reference                                   here
 ==========================================  ==========================================
 
 Top-k ties (equal fp32 scores) are ranked lower page index first; the
-reference leaves their order to ``torch.topk``.
+reference leaves their order to ``torch.topk``.  Traces are the reference's
+own ``QuestTrace`` / ``QuestSelection`` records (``quest.py:78-104``).
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
-
 import torch
+from qwenquest.quest import QuestSelection, QuestTrace  # the reference's own records
 
 from qwenquest_b200 import _lib
 from qwenquest_b200._lib import QQ_BF16, QQ_F32, QQ_STEP_FINALIZE, QQ_STEP_FOLD, check
@@ -45,35 +45,6 @@ def dtype_code(dtype: torch.dtype) -> int:
 
 def stream_of(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
-
-
-@dataclass
-class QuestSelection:
-    """One ``retrieve_topk`` decision (``quest.py:78-89``)."""
-
-    layer_id: int
-    req_pool_idx: int
-    seq_len: int
-    dense: bool
-    selected_pages: list[int]
-    recent_window: tuple[int, int]
-    page_scores: torch.Tensor | None
-    positions: torch.Tensor
-
-
-@dataclass
-class QuestTrace:
-    """Opt-in recorder (``quest.py:92-104``): ``quest.trace = QuestTrace()``."""
-
-    max_records: int | None = None
-    records: list[QuestSelection] = field(default_factory=list)
-
-    def add(self, record: QuestSelection) -> None:
-        if self.max_records is None or len(self.records) < self.max_records:
-            self.records.append(record)
-
-    def for_layer(self, layer_id: int) -> list[QuestSelection]:
-        return [r for r in self.records if r.layer_id == layer_id]
 
 
 class StepLayout:
