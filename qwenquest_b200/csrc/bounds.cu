@@ -137,13 +137,18 @@ struct StepArgs {
 template <typename T>
 __global__ void decode_step_kernel(StepArgs a) {
   wait_prior_grid();
-  allow_next_grid();
+  // The next kernel (a selection) may read the bounds before its own grid
+  // wait, so this kernel lets it launch only from its end, after its writes
+  // (allow_next_grid below).
   const int i = blockIdx.x;
   const int g = blockIdx.y;
   const qq_quest_state& st = a.st;
   const int64_t req = a.reqs[i];
   // a request index outside the state (or the table) is skipped: nothing of it is read or written
-  if (req < 0 || req >= st.max_reqs || (a.r2t != nullptr && a.r2t_rows > 0 && req >= a.r2t_rows)) return;
+  if (req < 0 || req >= st.max_reqs || (a.r2t != nullptr && a.r2t_rows > 0 && req >= a.r2t_rows)) {
+    allow_next_grid();
+    return;
+  }
   const int P = st.page_size;
   const bool skip = a.skip != nullptr && a.skip[req] != 0;
   const int count = st.running_token_count[req];
@@ -209,6 +214,8 @@ __global__ void decode_step_kernel(StepArgs a) {
       a.counters[i] = 0;
     }
   }
+  __threadfence();
+  allow_next_grid();
 }
 
 bool valid_state(const qq_quest_state* st) {

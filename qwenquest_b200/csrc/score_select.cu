@@ -296,17 +296,56 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
   __shared__ int s_digit, s_above, s_last, s_ngt;
   extern __shared__ __align__(16) unsigned char s_dyn[];  // the radix selection's keys and pages
 
+  const qq_quest_state& st = a.st;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nch = st.kv_heads * st.head_dim;
+  const int nvec = nch >> 2;
+  const size_t page_words = (size_t)nvec;  // 16-byte words per page
+  constexpr uint32_t kSlot = KW * 32 * 16;  // bytes of one page
+  const uint32_t ring = smem_u32(s_dyn) + (uint32_t)warp * (RING > 0 ? RING : 1) * kSlot + lane * 16;
+
+  // Before the grid wait: the block's first unit puts its warps' first
+  // RING - 1 pages in flight into the ring.  The bounds do not depend on
+  // the previous kernel (a fused attention, or the model's layers in an
+  // engine): the step's bounds fold wrote them, and it completed before
+  // that kernel started.  The previous attention's last blocks leave HBM
+  // partly idle, so these copies cost its tail little.
+  int pre_unit = -1;
+  if constexpr (RING > 0) {
+    if (!a.score_all && (int)blockIdx.x < a.units) {
+      const int u = blockIdx.x, i = u / a.parts, j = u - (u / a.parts) * a.parts;
+      const int64_t req = a.reqs[i], L = a.seq_lens[i];
+      if (req >= 0 && req < st.max_reqs && !(a.r2t != nullptr && a.r2t_rows > 0 && req >= a.r2t_rows) &&
+          L > st.top_k) {
+        int64_t F = L / st.page_size;
+        if (F > st.max_pages) F = st.max_pages;
+        const int64_t C = st.avoid_recent_overlap ? (F > 0 ? F - 1 : 0) : F;
+        const int64_t pg0 = (int64_t)j * C / a.parts, p_end = (int64_t)(j + 1) * C / a.parts;
+        const uint4* bounds = reinterpret_cast<const uint4*>(st.page_bounds) +
+                              ((size_t)a.layer * st.max_reqs + req) * st.max_pages * page_words;
+        const int64_t pw0 = pg0 + warp;
+        const int npages = p_end > pw0 ? (int)((p_end - pw0 + kWarps - 1) / kWarps) : 0;
+#pragma unroll
+        for (int d = 0; d < (RING > 0 ? RING - 1 : 0); ++d) {
+          if (d < npages) {
+            const uint4* src = bounds + (size_t)(pw0 + (int64_t)d * kWarps) * page_words;
+#pragma unroll
+            for (int it = 0; it < KW; ++it)
+              if (lane + 32 * it < nvec) cp_async_16(ring + d * kSlot + it * 512, src + lane + 32 * it);
+          }
+          cp_async_commit();
+        }
+        pre_unit = u;
+      }
+    }
+  }
+
   wait_prior_grid();
   // the call's epoch (thread 0 publishes): the counter is advanced only by
   // the previous call's attention (complete by now) and read by this call's
   // attention; the value is used only once a request is ready
   const uint32_t epoch = a.ready != nullptr && threadIdx.x == 0 ? ld_volatile_u32(a.call_counter) + 1 : 0u;
   allow_next_grid();
-  const qq_quest_state& st = a.st;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nch = st.kv_heads * st.head_dim;
-  const int nvec = nch >> 2;
-  const size_t page_words = (size_t)nvec;  // 16-byte words per page
   const int G = a.q_heads / st.kv_heads;
   const int D = st.head_dim;
   const int sel_req = st.top_k / st.page_size - 1;
@@ -386,8 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     };
     const int64_t pw0 = pg0 + warp;
     const int npages = p_end > pw0 ? (int)((p_end - pw0 + kWarps - 1) / kWarps) : 0;  // this warp's pages
-    constexpr uint32_t kSlot = KW * 32 * 16;  // bytes of one page
-    const uint32_t ring = smem_u32(s_dyn) + (uint32_t)warp * (RING > 0 ? RING : 1) * kSlot + lane * 16;
+    const bool prefetched = u == pre_unit;  // its first RING - 1 pages are in flight already
     auto copy_page = [&](int slot, int64_t p) {
       const uint4* src = bounds + (size_t)p * page_words;
 #pragma unroll
@@ -400,10 +438,12 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     // first scores (measured).
     constexpr int kPre = 1;
     if constexpr (RING > 0) {
+      if (!prefetched) {
 #pragma unroll
-      for (int d = 0; d < kPre; ++d) {
-        if (d < npages) copy_page(d, pw0 + (int64_t)d * kWarps);
-        cp_async_commit();
+        for (int d = 0; d < kPre; ++d) {
+          if (d < npages) copy_page(d, pw0 + (int64_t)d * kWarps);
+          cp_async_commit();
+        }
       }
     } else {
 #pragma unroll
@@ -436,10 +476,12 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
         if (c < nch) s_qbar[c] = G == 1 ? qsum[ci] : Elem<QT>::round(__fdiv_rn(qsum[ci], (float)G));
       }
       if constexpr (RING > 0) {
+        if (!prefetched) {
 #pragma unroll
-        for (int d = kPre; d < RING - 1; ++d) {
-          if (d < npages) copy_page(d, pw0 + (int64_t)d * kWarps);
-          cp_async_commit();
+          for (int d = kPre; d < RING - 1; ++d) {
+            if (d < npages) copy_page(d, pw0 + (int64_t)d * kWarps);
+            cp_async_commit();
+          }
         }
       }
       __syncthreads();
