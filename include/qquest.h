@@ -205,7 +205,8 @@ int qq_quest_extend_kv(const qq_quest_state* st, int layer, int write_counters,
 /* For every request i of the batch whose skip flag is clear: fold the key of
  * its previous token into the running bounds of layers [layer_begin,
  * layer_end) and/or finalize.  The previous token's row is rows[i] when rows
- * is given, else req_to_token[req][max(seq_len-2,0)] when table is given,
+ * is given (an entry of -1 takes no part: no fold, no finalize), else
+ * req_to_token[req][max(seq_len-2,0)] when table is given,
  * else req * (buf + 1) + min(seq_len - 2, buf).  skip_flags (device [max_reqs],
  * nullable) are read and cleared.  Replaces
  * QuestOnlyBackend._do_quest_decode_step_update (quest_only.py:84-97),
@@ -354,11 +355,46 @@ int qq_hisparse_reset(const qq_hisparse_state* hs, int req_pool_idx, void* strea
  * (coordinator.py:166-167). */
 int qq_hisparse_admit_layout(const qq_hisparse_state* hs, int req_pool_idx, void* stream);
 
+/* ---- [H1][H2][H4] host-tier rows handed out on the device ------------- */
+/* The host tier's free rows as a ring in device memory, the role of the
+ * reference's TokenToKVPoolAllocator over host indices (memory.py:53-76,
+ * coordinator.py:117): allocation takes rows from the head in ring order,
+ * freed rows go back at the tail, so rows come out in the reference's order
+ * and no host round trip is needed.  state[0] = head, state[1] = tail
+ * (allocation counts; free rows = tail - head). */
+typedef struct qq_host_ring {
+  int64_t* rows;     /* device [capacity] */
+  int64_t* state;    /* device [2]: head, tail */
+  int64_t capacity;  /* host rows 1 .. capacity */
+} qq_host_ring;
+/* All rows free, in order 1 .. capacity. */
+int qq_host_ring_init(const qq_host_ring* ring, void* stream);
+/* out[0 .. n) <- the next n free rows (TokenToKVPoolAllocator.alloc,
+ * memory.py:64-70); fewer free: the rest are -1 and err gets
+ * QQ_DEV_ERR_CAPACITY (the reference raises RuntimeError). */
+int qq_host_ring_alloc(const qq_host_ring* ring, int64_t n, int64_t* out, uint32_t* err, void* stream);
+/* Request req's host rows (req_to_host_pool[req] >= 0, in position order)
+ * back to the ring, entries reset to -1 (coordinator.py:310-312). */
+int qq_host_ring_free_request(const qq_hisparse_state* hs, int req_pool_idx, const qq_host_ring* ring,
+                              void* stream);
+/* [H2] The plan of HiSparseCoordinator.prepare_decode_step
+ * (coordinator.py:183-215) on the device: for each batch entry i whose
+ * request's skip flag (device [max_reqs], set at admission) is clear, the
+ * previous token (position seq_len - 2) gets a new host row from the ring,
+ * in batch order, recorded in req_to_host_pool; plan_dev[i] = its hot-buffer
+ * row req * (buf + 1) + min(seq_len - 2, buf), plan_host[i] = the host row
+ * (both -1 for an entry whose flag was set; the flag is cleared).  The bounds
+ * fold (qq_quest_decode_step with rows = plan_dev) and the backup
+ * (qq_copy_rows plan_dev -> plan_host, -1 entries skipped) follow. */
+int qq_hisparse_plan_step(const qq_hisparse_state* hs, const qq_batch* batch, uint8_t* skip_flags,
+                          const qq_host_ring* ring, int64_t* plan_dev, int64_t* plan_host, uint32_t* err,
+                          void* stream);
+
 /* ---- row copies (admission, eager backup) ----------------------------- */
 /* For every (layer, i < n): dst_layers[layer][dst_idx[i]] <- src_layers[layer][src_idx[i]],
  * row_bytes bytes per row; strides in bytes; index arrays int32 or int64
- * (idx_is64 != 0).  src/dst may be device memory or mapped pinned host
- * memory.  Used for HiSparse admission (coordinator.py:154-164) and the
+ * (idx_is64 != 0); an entry with a negative index is skipped.  src/dst may
+ * be device memory or mapped pinned host memory.  Used for HiSparse admission (coordinator.py:154-164) and the
  * eager host backup of the previous token (coordinator.py:211-215). */
 int qq_copy_rows(const void* const* src_layers, void* const* dst_layers, int num_layers,
                  int64_t src_row_stride, int64_t dst_row_stride, int64_t row_bytes,

@@ -101,6 +101,10 @@ class QQHotBuffer(ctypes.Structure):
     ]
 
 
+class QQHostRing(ctypes.Structure):
+    _fields_ = [("rows", c_void_p), ("state", c_void_p), ("capacity", c_int64)]
+
+
 class QQHiSparseState(ctypes.Structure):
     _fields_ = [
         ("buffer_tokens", c_void_p),
@@ -165,6 +169,11 @@ SIGNATURES: dict[str, tuple] = {
                 c_void_p]),
     "qq_hisparse_reset": (c_int, [_H, c_int, c_void_p]),
     "qq_hisparse_admit_layout": (c_int, [_H, c_int, c_void_p]),
+    "qq_host_ring_init": (c_int, [POINTER(QQHostRing), c_void_p]),
+    "qq_host_ring_alloc": (c_int, [POINTER(QQHostRing), c_int64, c_void_p, c_void_p, c_void_p]),
+    "qq_host_ring_free_request": (c_int, [_H, c_int, POINTER(QQHostRing), c_void_p]),
+    "qq_hisparse_plan_step": (
+        c_int, [_H, _B, c_void_p, POINTER(QQHostRing), c_void_p, c_void_p, c_void_p, c_void_p]),
     "qq_copy_rows": (
         c_int, [_PP, _PP, c_int, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int, c_int64, c_void_p]),
 }
@@ -236,6 +245,7 @@ __all__ = [
     "QQNewToken",
     "QQQuestState",
     "QQTokenTable",
+    "QQHostRing",
     "check",
     "load",
     "ptr_array",

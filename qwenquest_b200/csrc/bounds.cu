@@ -150,6 +150,11 @@ __global__ void decode_step_kernel(StepArgs a) {
     return;
   }
   const int P = st.page_size;
+  // a batch entry whose row is -1 (a HiSparse request on its first decode step) takes no part
+  if (a.rows != nullptr && a.rows[i] < 0) {
+    allow_next_grid();
+    return;
+  }
   const bool skip = a.skip != nullptr && a.skip[req] != 0;
   const int count = st.running_token_count[req];
   const int page = st.running_page_idx[req];

@@ -15,6 +15,8 @@
 
 #include <climits>
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace qq {
@@ -340,7 +342,144 @@ __global__ void copy_rows_kernel(CopyArgs a) {
   if (r >= a.n) return;
   const int64_t si = a.src64 ? static_cast<const int64_t*>(a.src_idx)[r] : static_cast<const int32_t*>(a.src_idx)[r];
   const int64_t di = a.dst64 ? static_cast<const int64_t*>(a.dst_idx)[r] : static_cast<const int32_t*>(a.dst_idx)[r];
+  if (si < 0 || di < 0) return;  // an entry with nothing to copy
   copy_row(a.dst[layer] + di * a.dst_stride, a.src[layer] + si * a.src_stride, a.row_bytes, lane);
+}
+
+// ------------------------------------------------------------------ host-tier rows on the device
+//
+// The host tier's free rows are a ring in device memory (the role of the
+// reference's TokenToKVPoolAllocator over host indices, memory.py:53-76):
+// rows[(c) % capacity] for allocation count c in [head, tail); allocation
+// takes from the head in ring order, a finished request's rows go back at
+// the tail in position order, so the order of rows handed out is the
+// reference's (its free list pops from the front and appends at the back).
+// head and tail only grow; everything runs on the device, in stream order.
+
+// Exclusive prefix sum of `v` over the block (blockDim.x a multiple of 32, <= 1024).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += t;
+    }
+    if (lane < nw) s_warp[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  const int before = warp > 0 ? s_warp[warp - 1] : 0;
+  total = s_warp[nw - 1];
+  __syncthreads();
+  return before + incl - v;
+}
+
+__global__ void ring_init_kernel(qq_host_ring r) {
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < r.capacity; k += (int64_t)gridDim.x * blockDim.x)
+    r.rows[k] = k + 1;  // rows 1 .. capacity (row 0 is padding)
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    r.state[0] = 0;
+    r.state[1] = r.capacity;
+  }
+}
+
+// n rows from the head into out (-1 and QQ_DEV_ERR_CAPACITY when fewer are free).
+__global__ void ring_alloc_kernel(qq_host_ring r, int64_t n, int64_t* out, uint32_t* err) {
+  const int64_t head = r.state[0], avail = r.state[1] - head;
+  for (int64_t k = threadIdx.x; k < n; k += blockDim.x) out[k] = k < avail ? r.rows[(head + k) % r.capacity] : -1;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (n > avail) raise_error(err, QQ_DEV_ERR_CAPACITY);
+    r.state[0] = head + (n < avail ? n : avail);
+  }
+}
+
+// A finished request's host rows (req_to_host_pool[req][p] >= 0, in position
+// order) go back to the ring's tail; the entries become -1.
+__global__ void ring_free_request_kernel(qq_hisparse_state hs, int req, qq_host_ring r) {
+  __shared__ int s_warp[32];
+  __shared__ int64_t s_tail;
+  int32_t* row = hs.req_to_host_pool + (int64_t)req * hs.max_context_len;
+  if (threadIdx.x == 0) s_tail = r.state[1];
+  __syncthreads();
+  for (int p0 = 0; p0 < hs.max_context_len; p0 += blockDim.x) {
+    const int p = p0 + threadIdx.x;
+    const int32_t h = p < hs.max_context_len ? row[p] : -1;
+    int total = 0;
+    const int rank = block_exclusive_scan(h >= 0 ? 1 : 0, s_warp, total);
+    if (h >= 0) {
+      r.rows[(s_tail + rank) % r.capacity] = h;
+      row[p] = -1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_tail += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) r.state[1] = s_tail;
+}
+
+// [H2] The per-step plan of HiSparseCoordinator.prepare_decode_step
+// (coordinator.py:183-215) without the host: for every batch entry whose
+// request is not on its first decode step (skip flag, cleared here), the
+// previous token (position seq_len - 2) is backed up from its hot-buffer row
+// req * (buf + 1) + min(seq_len - 2, buf) to a new host row taken from the
+// ring in batch order; req_to_host_pool records it.  plan_dev / plan_host
+// get those rows (-1 for a skipped entry) for the bounds fold and the copy.
+__global__ void plan_step_kernel(qq_hisparse_state hs, const int64_t* reqs, const int64_t* seq_lens, int bs,
+                                 uint8_t* skip, qq_host_ring r, int64_t* plan_dev, int64_t* plan_host,
+                                 uint32_t* err) {
+  __shared__ int s_warp[32];
+  __shared__ int64_t s_head, s_avail;
+  if (threadIdx.x == 0) {
+    s_head = r.state[0];
+    s_avail = r.state[1] - s_head;
+  }
+  __syncthreads();
+  const int64_t buf = hs.device_buffer_size;
+  int64_t taken = 0;
+  for (int i0 = 0; i0 < bs; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
+    bool need = false;
+    int64_t req = -1, prev = 0;
+    if (i < bs) {
+      req = reqs[i];
+      if (req < 0 || req >= hs.max_reqs) {
+        raise_error(err, QQ_DEV_ERR_BOUNDS);
+      } else if (skip[req]) {
+        skip[req] = 0;
+      } else {
+        prev = seq_lens[i] - 2;
+        need = prev >= 0 && prev < hs.max_context_len;
+      }
+    }
+    int total = 0;
+    const int64_t rank = taken + block_exclusive_scan(need ? 1 : 0, s_warp, total);
+    if (i < bs) {
+      int64_t dev = -1, host = -1;
+      if (need) {
+        if (rank < s_avail) {
+          dev = req * (buf + 1) + (prev < buf ? prev : buf);
+          host = r.rows[(s_head + rank) % r.capacity];
+          hs.req_to_host_pool[req * hs.max_context_len + prev] = (int32_t)host;
+        } else {
+          raise_error(err, QQ_DEV_ERR_CAPACITY);
+        }
+      }
+      plan_dev[i] = dev;
+      plan_host[i] = host;
+    }
+    taken += total;
+  }
+  if (threadIdx.x == 0) r.state[0] = s_head + (taken < s_avail ? taken : s_avail);
 }
 
 bool valid_hs(const qq_hisparse_state* hs) {
@@ -436,6 +575,45 @@ extern "C" int qq_copy_rows(const void* const* src_layers, void* const* dst_laye
   const int warps = 8;
   dim3 grid((unsigned)((n + warps - 1) / warps), num_layers);
   copy_rows_kernel<<<grid, warps * 32, 0, as_stream(stream)>>>(a);
+  return launch_status();
+}
+
+
+static bool valid_ring(const qq_host_ring* r) {
+  return r != nullptr && r->rows != nullptr && r->state != nullptr && r->capacity > 0;
+}
+
+extern "C" int qq_host_ring_init(const qq_host_ring* ring, void* stream) {
+  if (!valid_ring(ring)) return QQ_ERR_INVALID;
+  const int64_t blocks = std::min<int64_t>((ring->capacity + 255) / 256, 4096);
+  ring_init_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(*ring);
+  return launch_status();
+}
+
+extern "C" int qq_host_ring_alloc(const qq_host_ring* ring, int64_t n, int64_t* out, uint32_t* err, void* stream) {
+  if (!valid_ring(ring) || n < 0 || (n > 0 && out == nullptr)) return QQ_ERR_INVALID;
+  if (n == 0) return QQ_OK;
+  ring_alloc_kernel<<<1, 1024, 0, as_stream(stream)>>>(*ring, n, out, err);
+  return launch_status();
+}
+
+extern "C" int qq_host_ring_free_request(const qq_hisparse_state* hs, int req, const qq_host_ring* ring,
+                                         void* stream) {
+  if (!valid_hs(hs) || !valid_ring(ring) || req < 0 || req >= hs->max_reqs) return QQ_ERR_INVALID;
+  ring_free_request_kernel<<<1, 1024, 0, as_stream(stream)>>>(*hs, req, *ring);
+  return launch_status();
+}
+
+extern "C" int qq_hisparse_plan_step(const qq_hisparse_state* hs, const qq_batch* batch, uint8_t* skip_flags,
+                                     const qq_host_ring* ring, int64_t* plan_dev, int64_t* plan_host, uint32_t* err,
+                                     void* stream) {
+  if (!valid_hs(hs) || !valid_ring(ring) || batch == nullptr || skip_flags == nullptr || plan_dev == nullptr ||
+      plan_host == nullptr)
+    return QQ_ERR_INVALID;
+  if (batch->bs == 0) return QQ_OK;
+  if (batch->bs < 0 || batch->bs > QQ_MAX_BS || !batch->req_pool_indices || !batch->seq_lens) return QQ_ERR_INVALID;
+  plan_step_kernel<<<1, 1024, 0, as_stream(stream)>>>(*hs, batch->req_pool_indices, batch->seq_lens, batch->bs,
+                                                      skip_flags, *ring, plan_dev, plan_host, err);
   return launch_status();
 }
 

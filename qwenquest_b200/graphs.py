@@ -19,8 +19,9 @@ Inside the graph the backend makes the same call per layer as eagerly: the
 fused ``qq_quest_decode_attention`` (selection and attention, the attention
 starting on each request as soon as its rows are written), whose per-call
 epoch is kept on the device and so is renewed on every replay; with
-``backend.fused = False`` the two calls.  The HiSparse backend's step reads
-the batch on the host (its host-row free list), so it is not captured.
+``backend.fused = False`` the two calls.  A HiSparse (Mode 3) step is
+captured the same way: its per-step plan, bounds fold and host backup, and
+per layer the selection, the swap-in and the attention, all on the device.
 """
 
 from __future__ import annotations
@@ -28,7 +29,7 @@ from __future__ import annotations
 import torch
 from qwenquest.batch import ForwardBatch, ForwardMode
 
-from .backends import B200QuestOnlyBackend
+from .backends import B200QuestHiSparseBackend, B200QuestOnlyBackend
 
 __all__ = ["DecodeStepGraph"]
 
@@ -41,10 +42,10 @@ class DecodeStepGraph:
     the backend's state advances only on ``replay``.
     """
 
-    def __init__(self, backend: B200QuestOnlyBackend, layers, batch: ForwardBatch, q, k, v, *,
-                 stack_outputs: bool = False):
-        if not isinstance(backend, B200QuestOnlyBackend):
-            raise TypeError("DecodeStepGraph captures B200QuestOnlyBackend decode steps")
+    def __init__(self, backend: B200QuestOnlyBackend | B200QuestHiSparseBackend, layers, batch: ForwardBatch,
+                 q, k, v, *, stack_outputs: bool = False):
+        if not isinstance(backend, (B200QuestOnlyBackend, B200QuestHiSparseBackend)):
+            raise TypeError("DecodeStepGraph captures B200QuestOnlyBackend / B200QuestHiSparseBackend decode steps")
         if backend.quest.trace is not None or backend.kernel_events is not None:
             raise ValueError("a traced or per-kernel-timed backend copies to the host every layer")
         dev = backend.device
@@ -55,7 +56,8 @@ class DecodeStepGraph:
         self.v = v.detach().clone()
         self.req_pool_indices = batch.req_pool_indices.to(device=dev, dtype=torch.int64).clone()
         self.seq_lens = batch.seq_lens.to(device=dev, dtype=torch.int64).clone()
-        self.out_cache_loc = batch.out_cache_loc.to(device=dev, dtype=torch.int64).clone()
+        self.out_cache_loc = (None if batch.out_cache_loc is None else
+                              batch.out_cache_loc.to(device=dev, dtype=torch.int64).clone())
         bs = int(self.req_pool_indices.shape[0])
         self.batch = ForwardBatch(
             forward_mode=ForwardMode.DECODE,
@@ -81,7 +83,8 @@ class DecodeStepGraph:
         if batch is not None:
             self.req_pool_indices.copy_(batch.req_pool_indices, non_blocking=True)
             self.seq_lens.copy_(batch.seq_lens, non_blocking=True)
-            self.out_cache_loc.copy_(batch.out_cache_loc, non_blocking=True)
+            if self.out_cache_loc is not None:
+                self.out_cache_loc.copy_(batch.out_cache_loc, non_blocking=True)
         for dst, src in ((self.q, q), (self.k, k), (self.v, v)):
             if src is not None:
                 dst.copy_(src, non_blocking=True)

@@ -13,9 +13,11 @@ Two tiers, as in the reference:
 The swap-in (dedupe, hit detection, eviction, host->device copy, LRU
 rewrite, row lookup) is one kernel launch per layer (``qq_hisparse_swap_in``);
 the eager host backup of the previous token and admission copies are
-``qq_copy_rows`` launches.  The host-row free list stays on the host, as in
-the reference, so ``prepare_decode_step`` reads the batch's request ids and
-lengths on the host once per step.
+``qq_copy_rows`` launches.  The host tier's free rows are a ring in device
+memory (:class:`DeviceHostRows`, the reference's ``TokenToKVPoolAllocator``
+API), so ``prepare_decode_step`` is three launches (the step plan, the bounds
+fold, the backup copy) with no host round trip, and a whole decode step can
+be captured in a CUDA graph.
 """
 
 from __future__ import annotations
@@ -27,10 +29,9 @@ import torch
 
 from qwenquest_b200 import _lib
 from qwenquest_b200._lib import QQ_STEP_FINALIZE, QQ_STEP_FOLD, check
-from qwenquest.memory import TokenToKVPoolAllocator
 from qwenquest_b200.quest import QuestAlgorithm, dtype_code, stream_of
 
-__all__ = ["HiSparseCoordinator", "SwapInStats"]
+__all__ = ["DeviceHostRows", "HiSparseCoordinator", "SwapInStats"]
 
 
 class SwapInStats:
@@ -67,6 +68,56 @@ def host_device_pointer(t: torch.Tensor) -> int:
     out = ctypes.c_void_p()
     check(_lib.load().qq_host_device_pointer(t.data_ptr(), ctypes.byref(out)), "host_device_pointer")
     return int(out.value)
+
+
+_DeviceErrorLike = "_DeviceError"
+
+
+class DeviceHostRows:
+    """The host tier's free rows (1 .. size) as a ring in device memory.
+
+    The API of the reference's ``TokenToKVPoolAllocator`` over host indices
+    (``memory.py:53-76``, used at ``coordinator.py:117``): ``alloc`` hands out
+    rows from the front of the free list and freed rows go to its back, in
+    the same order, but the list lives on the device, so allocating in a
+    decode step needs no host round trip.  ``alloc`` returns a device tensor
+    at once; running out is reported through the coordinator's device error
+    word (``RuntimeError`` at its next check) instead of raising here.
+    ``available_size`` reads the device and so synchronizes.
+    """
+
+    def __init__(self, size: int, device: torch.device, err: _DeviceErrorLike):
+        self.size = size
+        self.device = device
+        self.lib = _lib.load()
+        self._err = err
+        self.rows = torch.empty(max(size, 1), dtype=torch.int64, device=device)
+        self.state = torch.zeros(2, dtype=torch.int64, device=device)  # head, tail
+        self.ring = _lib.QQHostRing(self.rows.data_ptr(), self.state.data_ptr(), size)
+        if size > 0:
+            check(self.lib.qq_host_ring_init(ctypes.byref(self.ring), stream_of(device)), "host ring init")
+
+    def available_size(self) -> int:
+        head, tail = self.state.tolist()
+        return int(tail - head)
+
+    def alloc(self, n: int) -> torch.Tensor:
+        out = torch.empty(int(n), dtype=torch.int64, device=self.device)
+        check(self.lib.qq_host_ring_alloc(ctypes.byref(self.ring), int(n), out.data_ptr(), self._err.ptr(),
+                                          stream_of(self.device)), "host rows alloc")
+        return out
+
+    def free(self, indices: torch.Tensor) -> None:
+        """Rows back to the end of the free list (synchronizes; the decode path frees per request on the device)."""
+        idx = indices.to(device=self.device, dtype=torch.int64).flatten()
+        idx = idx[idx > 0]
+        n = int(idx.numel())
+        if not n:
+            return
+        tail = int(self.state[1])
+        pos = (tail + torch.arange(n, device=self.device)) % self.size
+        self.rows[pos] = idx
+        self.state[1] = tail + n
 
 
 @dataclass
@@ -134,8 +185,9 @@ class HiSparseCoordinator:
         self.max_reqs, self.max_context_len = max_reqs, max_context_len
         dev = self.device
 
-        # ---- host tier (pinned, device-mapped)
-        self.host_allocator = TokenToKVPoolAllocator(host_pool_size, device="cpu")
+        # ---- host tier (pinned, device-mapped); its free rows on the device
+        self._err = _DeviceError(torch.zeros(1, dtype=torch.int32).pin_memory())
+        self.host_allocator = DeviceHostRows(host_pool_size, dev, self._err)
         hshape = (host_pool_size + 1, kv_heads, head_dim)
         # host_layers < num_layers aliases layer l onto host buffer l % host_layers
         # (benchmarks whose full host history would not fit in host RAM)
@@ -156,11 +208,13 @@ class HiSparseCoordinator:
         self.buffer_tokens = torch.full((num_layers, max_reqs, buf), -1, dtype=torch.int32, device=dev)
         self._lru_init = torch.arange(buf, dtype=torch.int32, device=dev)
         self.lru_slots = self._lru_init.repeat(num_layers, max_reqs, 1).contiguous()
-        self._skip_first_backup = [False] * max_reqs
+        # set at admission, cleared by the first decode step (no previous token to back up yet)
+        self._skip_first_backup = torch.zeros(max_reqs, dtype=torch.uint8, device=dev)
+        self._plan_dev = torch.empty(max_reqs, dtype=torch.int64, device=dev)
+        self._plan_host = torch.empty(max_reqs, dtype=torch.int64, device=dev)
         self._backup_stream: torch.cuda.Stream | None = None
         self._stats = torch.zeros(3, dtype=torch.int64, device=dev)
         self.stats = SwapInStats(self._stats)
-        self._err = _DeviceError(torch.zeros(1, dtype=torch.int32).pin_memory())
         self._hs = _lib.QQHiSparseState(
             self.buffer_tokens.data_ptr(), self.lru_slots.data_ptr(), self.req_to_host_pool.data_ptr(),
             self._stats.data_ptr(), num_layers, max_reqs, max_context_len, buf, top_k,
@@ -185,8 +239,7 @@ class HiSparseCoordinator:
         req = int(req_pool_idx)
         n = int(prefill_len)
         idx = prefill_indices.to(device=self.device, dtype=torch.int32).contiguous()
-        host_idx = self.host_allocator.alloc(n)
-        host_idx_dev = host_idx.to(self.device)
+        host_idx_dev = self.host_allocator.alloc(n)
         self.req_to_host_pool[req, :n] = host_idx_dev.to(torch.int32)
         n_dev = min(n, self.device_buffer_size)
         kb = [token_to_kv_pool.get_key_buffer(layer) for layer in range(self.num_layers)]
@@ -206,7 +259,7 @@ class HiSparseCoordinator:
         check(self.lib.qq_hisparse_admit_layout(self._hs, req, s), "admit_request layout")
         q = self.quest
         q.update_prefill_representations_all_layers(req, kb[q.start_layer:q.end_layer], idx)
-        self._skip_first_backup[req] = True
+        self._skip_first_backup[req] = 1
         del keep
 
     # ------------------------------------ [H1] admission fused with the prefill
@@ -223,7 +276,7 @@ class HiSparseCoordinator:
         """
         src, dst = [], []
         for req, n in zip(reqs, seq_lens, strict=True):
-            host_idx_dev = self.host_allocator.alloc(n).to(self.device)
+            host_idx_dev = self.host_allocator.alloc(n)
             self.req_to_host_pool[req, :n] = host_idx_dev.to(torch.int32)
             src.append(req_to_token[req, :n].to(torch.int32))
             dst.append(host_idx_dev.to(torch.int64))
@@ -257,7 +310,7 @@ class HiSparseCoordinator:
         s = self._stream()
         for req in adm.reqs:
             check(self.lib.qq_hisparse_admit_layout(self._hs, req, s), "admit_request layout")
-            self._skip_first_backup[req] = True
+        self._skip_first_backup[torch.tensor(adm.reqs, dtype=torch.int64).to(self.device, non_blocking=True)] = 1
 
     # -------------------------------------------------- [H2] per decode step
 
@@ -265,32 +318,34 @@ class HiSparseCoordinator:
         return (seq_lens.long() - 1).clamp(max=self.device_buffer_size)
 
     def prepare_decode_step(self, req_pool_indices: torch.Tensor, seq_lens: torch.Tensor) -> None:
-        """[H2] (coordinator.py:183-215): fold the previous token's key into the bounds, back it up."""
-        self.check_errors()
-        backup_reqs: list[int] = []
-        backup_pos: list[int] = []
-        for req, seq_len in zip(req_pool_indices.tolist(), seq_lens.tolist(), strict=True):
-            if self._skip_first_backup[req]:
-                self._skip_first_backup[req] = False
-                continue
-            backup_reqs.append(req)
-            backup_pos.append(seq_len - 2)
-        if not backup_reqs:
+        """[H2] (coordinator.py:183-215): fold the previous token's key into the bounds, back it up.
+
+        Three launches and no host round trip: the step plan (skip flags, a
+        new host row per request from the device free list, in batch order,
+        ``req_to_host_pool``), the bounds fold of the previous token (all
+        layers) and its K/V copy from the hot buffer to the host tier.
+        """
+        dev = self.device
+        reqs = req_pool_indices.to(device=dev, dtype=torch.int64).contiguous()
+        seq = seq_lens.to(device=dev, dtype=torch.int64).contiguous()
+        bs = int(reqs.shape[0])
+        if bs == 0:
             return
-        buf = self.device_buffer_size
-        dev_locs_l = [r * (buf + 1) + min(p, buf) for r, p in zip(backup_reqs, backup_pos)]
-        host_idx = self.host_allocator.alloc(len(backup_reqs))
-        packed = torch.tensor([backup_reqs, backup_pos, dev_locs_l, host_idx.tolist()], dtype=torch.int64)
-        packed = packed.pin_memory().to(self.device, non_blocking=True)
-        reqs, prev_pos, dev_locs, host_dev = packed[0], packed[1], packed[2], packed[3]
+        if bs > self.max_reqs:
+            raise ValueError(f"batch of {bs} requests exceeds max_reqs ({self.max_reqs})")
+        s = self._stream()
+        batch = _lib.QQBatch(reqs.data_ptr(), seq.data_ptr(), bs)
+        check(self.lib.qq_hisparse_plan_step(self._hs, batch, self._skip_first_backup.data_ptr(),
+                                             ctypes.byref(self.host_allocator.ring), self._plan_dev.data_ptr(),
+                                             self._plan_host.data_ptr(), self._err.ptr(), s),
+              "decode step plan")
         q = self.quest
-        q.decode_step(QQ_STEP_FOLD | QQ_STEP_FINALIZE, reqs, None, None, rows=dev_locs,
+        q.decode_step(QQ_STEP_FOLD | QQ_STEP_FINALIZE, reqs, None, None, rows=self._plan_dev,
                       k_ptrs=self._dev_k_ptrs[0], kv_dtype=dtype_code(self.dtype),
                       k_row_stride=self.kv_heads * self.head_dim)
-        self.req_to_host_pool[reqs, prev_pos] = host_dev.to(torch.int32)
         check(self.lib.qq_copy_rows(self._dev_ptrs[0], self._host_ptrs[0], 2 * self.num_layers, self.row_bytes,
-                                    self.row_bytes, self.row_bytes, dev_locs.data_ptr(), 1, host_dev.data_ptr(),
-                                    1, len(backup_reqs), self._stream()),
+                                    self.row_bytes, self.row_bytes, self._plan_dev.data_ptr(), 1,
+                                    self._plan_host.data_ptr(), 1, bs, s),
               "eager host backup")
 
     def write_new_token(self, layer_id, req_pool_indices, seq_lens, k, v) -> None:
@@ -307,7 +362,7 @@ class HiSparseCoordinator:
         batch = _lib.QQBatch(reqs.data_ptr(), seq_lens.data_ptr(), bs)
         rc = self.lib.qq_hisparse_swap_in(
             self._hs, int(layer_id), batch, positions.data_ptr(), rows_out.data_ptr(),
-            host_device_pointer(self.host_k[layer_id]), host_device_pointer(self.host_v[layer_id]),
+            self._host_dev[layer_id], self._host_dev[self.num_layers + layer_id],
             self.device_k[layer_id].data_ptr(), self.device_v[layer_id].data_ptr(), self.row_bytes,
             self._err.ptr(), self._stream(),
         )
@@ -336,12 +391,13 @@ class HiSparseCoordinator:
     # -------------------------------------------------- [H4] release
 
     def request_finished(self, req_pool_idx: int) -> None:
-        """[H4] (coordinator.py:308-316)."""
+        """[H4] (coordinator.py:308-316), on the device: the host rows go back to the free list."""
         req = int(req_pool_idx)
-        host_idx = self.req_to_host_pool[req].cpu()
-        self.host_allocator.free(host_idx[host_idx >= 0].to(torch.int64))
-        check(self.lib.qq_hisparse_reset(self._hs, req, self._stream()), "request_finished")
-        self._skip_first_backup[req] = False
+        s = self._stream()
+        check(self.lib.qq_host_ring_free_request(self._hs, req, ctypes.byref(self.host_allocator.ring), s),
+              "request_finished host rows")
+        check(self.lib.qq_hisparse_reset(self._hs, req, s), "request_finished")
+        self._skip_first_backup[req] = 0
         self.quest.invalidate_request(req)
 
     # -------------------------------------------------- introspection
@@ -352,5 +408,3 @@ class HiSparseCoordinator:
     def host_bytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in {id(t): t for t in self.host_k + self.host_v}.values())
 
-
-_ = ctypes

@@ -171,7 +171,7 @@ def test_hisparse_admission_fused_equals_reference_order(dtype, kv, d, cuda_devi
             assert torch.equal(getattr(ca, name)[li], getattr(cb, name)[li]), (name, li)
     assert torch.equal(ca.buffer_tokens, cb.buffer_tokens)
     assert torch.equal(ca.lru_slots, cb.lru_slots)
-    assert ca._skip_first_backup == cb._skip_first_backup
+    assert torch.equal(ca._skip_first_backup, cb._skip_first_backup)
     # the host tier holds every prefill position's K/V, the hot buffer positions [0, BUF)
     pool = runs[0].pool
     for r, n in zip(reqs, new, strict=True):
