@@ -23,8 +23,9 @@ the host cores, CPU pools) on config 1's 64-request batch, one layer per step
 it; the GPU arm's ``cpu_baseline`` is the same measurement.
 
 Other single-GPU cases, each printing its own JSON line (not the headline):
-``--case prefill`` (one 32K-token prefill's K/V write + Quest bounds over 48
-layers, fused against the reference's order), ``--case config2`` (16 ragged
+``--case config0`` (one 8K-token request, one layer: microseconds per
+layer-step), ``--case prefill`` (one 32K-token prefill's K/V write + Quest
+bounds over 48 layers, fused against the reference's order), ``--case config2`` (16 ragged
 requests up to 131K tokens, Mode 2) and ``--case config3`` (HiSparse, 32
 requests at 65,536 tokens with the host tier, against the host-link
 roofline).  ``--context-limit`` runs config 1 under a larger engine
@@ -589,6 +590,86 @@ def config3_case(args) -> None:
     }), flush=True)
 
 
+# --------------------------------------------------------------------------- config 0
+
+
+def config0_case(args) -> None:
+    """``--case config0``: one request with an 8 192-token prefix (L = 8193, 128 candidate pages), one layer.
+
+    4,495,360 algorithmic bytes per layer-step (under a microsecond at HBM
+    speed): latency-bound, so the line reports microseconds per layer-step
+    (lower is better) for the captured step (``DecodeStepGraph``: the step's
+    bounds fold + the fused selection / attention call), the eager calls, and
+    per kernel.  K, V = N(0,1) x LogNormal(0,0.5) per channel, q N(0,1); the
+    benchmark's four planted pages move only the selection, not the work.
+    """
+    from qwenquest_b200.graphs import DecodeStepGraph
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    prefix, steps, warm = 8192, max(args.steps, 100), args.warmup
+    total = 2 * (warm + steps) + warm + 5 + 2
+    backend, pool, r2t, max_ctx, qkv = build_config1(dev, total, args.seed, n_req=1, prefix=prefix, layers=1,
+                                                     resident=1)
+    batches, layers = make_batches(dev, backend, pool, r2t, max_ctx, total, n_req=1, prefix=prefix)
+    qs, ks, vs = qkv
+    cur = [0]
+
+    def take(n):
+        cur[0] += n
+        return range(cur[0] - n, cur[0])
+
+    def timed(run, rng):
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for st in rng:
+            run(st)
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) * 1e3 / len(rng)  # us per step
+
+    eager = lambda st: run_step(backend, batches[st], layers, qkv)  # noqa: E731
+    for st in take(warm):
+        eager(st)
+    eager_us = timed(eager, take(steps))
+    graph = DecodeStepGraph(backend, layers, batches[cur[0]], qs, ks, vs)
+    replay = lambda st: graph.replay(batches[st])  # noqa: E731
+    for st in take(warm):
+        replay(st)
+    clocks = ClockSampler(0)
+    clocks.start()
+    graph_us = timed(replay, take(steps))
+    clock_info = clocks.stop()
+    kernel_ms = _kernel_ms(backend, batches, layers, qkv_steps(qkv, total), *_span(take(5)))
+    backend.check_errors()
+    step_bytes = 4_233_216 + 2048 * (prefix // PAGE)
+    print(json.dumps({
+        "case": "config0", "metric": "Quest sparse-decode latency per layer-step (1 request)", "value": graph_us,
+        "unit": "us", "n_gpus": 1, "steps": steps, "warmup": warm, "ms_per_step": graph_us / 1e3,
+        "higher_is_better": False, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) x LogNormal(0,0.5) per-channel K/V, N(0,1) q)",
+        "config": {"workload": "config0: 1 request x 8192-token prefix (L = 8193, 128 candidate pages), 1 layer, "
+                               "Quest top_k 2048 / page 64, Qwen3-30B-A3B attention (32q/4kv x 128, bf16)",
+                   "layer_step_bytes": step_bytes,
+                   "l2": "one request: ~4.5 MB per layer-step stays in L2 between steps (latency case)"},
+        "paths": {"graph_us": graph_us, "eager_us": eager_us,
+                  "what": "per layer-step: the step's bounds fold + one fused selection / attention call"},
+        "kernel_us": {k: v * 1e3 for k, v in kernel_ms.items()},
+        "layer_step_gbs": step_bytes / (graph_us * 1e-6) / 1e9,
+        "clocks": clock_info,
+    }), flush=True)
+
+
+def qkv_steps(qkv, total):
+    """The same per-layer inputs for every step ([steps, layers, ...] views)."""
+    return tuple(t.unsqueeze(0).expand(total, *t.shape) for t in qkv)
+
+
+def _span(rng):
+    return rng.start, rng.stop
+
+
 # --------------------------------------------------------------------------- CPU baseline
 
 
@@ -774,7 +855,7 @@ def main() -> None:
     ap.add_argument("--resident", type=int, default=RESIDENT, help="physical KV buffers")
     ap.add_argument("--context-limit", type=int, default=None,
                     help="engine max_context_len above the requests' lengths (profiling cases only)")
-    ap.add_argument("--case", choices=["decode", "prefill", "config2", "config3"], default="decode",
+    ap.add_argument("--case", choices=["decode", "prefill", "config0", "config2", "config3"], default="decode",
                     help="decode: the benchmark, config 1 (default); prefill: the prefill K/V write + bounds; "
                          "config2 / config3: the ragged and HiSparse benchmark configs (1 GPU each)")
     ap.add_argument("--path", choices=["graph", "eager"], default="graph",
@@ -785,7 +866,8 @@ def main() -> None:
     args.warmup = max(args.warmup, 3)
     if args.case != "decode":
         if int(os.environ.get("RANK", "0")) == 0:
-            {"prefill": prefill_case, "config2": config2_case, "config3": config3_case}[args.case](args)
+            {"prefill": prefill_case, "config0": config0_case, "config2": config2_case,
+             "config3": config3_case}[args.case](args)
         return
     from qwenquest_b200.graphs import DecodeStepGraph
     from qwenquest_b200.sharding import max_over_ranks, shard_requests
