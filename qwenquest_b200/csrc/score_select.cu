@@ -69,12 +69,24 @@ struct SelectArgs {
 };
 
 // Request i's layout is written (by the whole block, before a barrier): its
-// ready word takes this launch's epoch, after a fence, for a consumer that
-// spins on it instead of waiting for the whole grid.
+// ready word takes this launch's epoch for a consumer that spins on it
+// instead of waiting for the whole grid.  The barrier orders the block's
+// writes before this thread's release store, which is cumulative over them.
 __device__ __forceinline__ void publish_ready(const SelectArgs& a, int i, uint32_t epoch) {
   if (a.ready == nullptr) return;
-  __threadfence();
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.ready + i), "r"(epoch) : "memory");
+}
+
+// Arrival of a part on request i's counter (acq_rel: the block's writes,
+// ordered by the preceding barrier, are released; the last arriver's later
+// reads of the other parts' writes are acquired).  True for the last part,
+// which resets the counter for the next launch.
+__device__ __forceinline__ bool arrive_last(int32_t* counter, int parts) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+  const bool last = old == parts - 1;
+  if (last) *counter = 0;
+  return last;
 }
 
 // Dynamic shared memory of the selection: order keys of the candidate
@@ -587,20 +599,12 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
           for (int off = 0; off < 4 * st.page_size; off += 128)
             asm volatile("prefetch.global.L2 [%0];" ::"l"(src + off));
         }
-        // publish the part's list; the barrier and thread 0's fence order
-        // every thread's writes before the arrival, the last arriver's fence
-        // orders its reads after it
+        // publish the part's list; the barrier and thread 0's acq_rel
+        // arrival order every thread's writes before it, and the last
+        // arriver's reads of the other lists after it
         if (warp == 0) a.lists[(size_t)u * kSelectListLen + lane] = top;
         __syncthreads();
-        if (tid == 0) {
-          __threadfence();
-          const bool last = atomicAdd(&a.counters[i], 1) == a.parts - 1;
-          if (last) {
-            __threadfence();
-            a.counters[i] = 0;
-          }
-          s_last = last;
-        }
+        if (tid == 0) s_last = arrive_last(a.counters + i, a.parts);
         __syncthreads();
         if (!s_last) continue;
         const uint64_t* plist = a.lists + (size_t)i * a.parts * kSelectListLen + lane;
@@ -645,15 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
     // (c) sel > 32: the block arrives on the request's counter; the last
     // part to arrive does the radix selection.
     __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      const bool last = atomicAdd(&a.counters[i], 1) == a.parts - 1;
-      if (last) {
-        __threadfence();
-        a.counters[i] = 0;
-      }
-      s_last = last;
-    }
+    if (tid == 0) s_last = arrive_last(a.counters + i, a.parts);
     __syncthreads();
     if (s_last) select_request(a, i, req, L, C, is_long, s_dyn, s_hist, s_digit, s_above, s_ngt);
     __syncthreads();  // the selection's shared memory is free again
