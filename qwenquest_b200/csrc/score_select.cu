@@ -609,7 +609,9 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
         if (!s_last) continue;
         const uint64_t* plist = a.lists + (size_t)i * a.parts * kSelectListLen + lane;
         if (a.parts <= 4) {
-          // warp 0 merges its own list with the other parts' (loaded together)
+          // warp 0 merges its own list with the other parts' (loaded
+          // together); with four parts the two merges that do not depend on
+          // each other run side by side
           if (warp == 0) {
             uint64_t x[3];
 #pragma unroll
@@ -617,14 +619,17 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
               const int jj = e < j ? e : e + 1;  // the other parts
               x[e] = jj < a.parts ? __ldcg(plist + (size_t)jj * kSelectListLen) : 0ull;
             }
-#pragma unroll
-            for (int e = 0; e < 3; ++e) top = top32_merge(top, x[e], lane);
+            uint64_t y = x[0];
+            if (a.parts > 2) y = top32_merge(x[0], x[1], lane);
+            if (a.parts > 3) top = top32_merge(top, x[2], lane);
+            top = top32_merge(top, y, lane);
           }
         } else {
           // warp w takes lists w, w + 16, ... (four loads in flight at a
-          // time), then the merge tree joins the warps (two barriers since
-          // every warp read the first tree's result)
+          // time; only real lists are merged, the first one taken as it is),
+          // then the merge tree joins the warps
           uint64_t mine = 0;
+          bool have = false;
           for (int j0 = warp; j0 < a.parts; j0 += 4 * kWarps) {
             uint64_t x[4];
 #pragma unroll
@@ -633,7 +638,12 @@ __global__ void __launch_bounds__(kThreads, 1) score_select_kernel(SelectArgs a)
               x[e] = jj < a.parts ? __ldcg(plist + (size_t)jj * kSelectListLen) : 0ull;
             }
 #pragma unroll
-            for (int e = 0; e < 4; ++e) mine = top32_merge(mine, x[e], lane);
+            for (int e = 0; e < 4; ++e) {
+              if (j0 + e * kWarps < a.parts) {
+                mine = have ? top32_merge(mine, x[e], lane) : x[e];
+                have = true;
+              }
+            }
           }
           top = block_top32(mine);
         }
