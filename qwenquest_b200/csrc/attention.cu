@@ -40,6 +40,13 @@
 namespace qq {
 namespace {
 
+// QQ_ATTN_FMA=1 builds the streaming kernel's per-stage contraction with fp32
+// FMA instead of mma.sync (for the measured comparison of the two; the
+// library ships the MMA build).
+#ifndef QQ_ATTN_FMA
+#define QQ_ATTN_FMA 0
+#endif
+
 // ------------------------------------------------------------------ fast path constants
 constexpr int kD = 128;
 constexpr int kKV = 4;
@@ -381,6 +388,19 @@ __device__ __forceinline__ void stream_share(const AttnArgs& a, uint32_t epoch, 
     if (cc.s_first) {
       // a new portion of a segment: Q^T fragments of this KV head, loaded
       // before the wait so their latency hides behind it
+#if QQ_ATTN_FMA
+      // query head gid, channels [32 tig, 32 tig + 32) as bf16 pairs
+      const uint4* q4 = reinterpret_cast<const uint4*>(qbase + (int64_t)cc.s_req * a.q_stride +
+                                                       (cc.s_head * kG + gid) * kD + 32 * tig);
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const uint4 w = __ldg(q4 + c4);
+        qb[2 * c4][0] = w.x;
+        qb[2 * c4][1] = w.y;
+        qb[2 * c4 + 1][0] = w.z;
+        qb[2 * c4 + 1][1] = w.w;
+      }
+#else
       const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qbase + (int64_t)cc.s_req * a.q_stride +
                                                                (cc.s_head * kG + gid) * kD);
 #pragma unroll
@@ -388,6 +408,7 @@ __device__ __forceinline__ void stream_share(const AttnArgs& a, uint32_t epoch, 
         qb[kk][0] = __ldg(qrow + (kk * 16 + 2 * tig) / 2);
         qb[kk][1] = __ldg(qrow + (kk * 16 + 8 + 2 * tig) / 2);
       }
+#endif
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
       m_a = m_b = kNegInf;
@@ -406,6 +427,71 @@ __device__ __forceinline__ void stream_share(const AttnArgs& a, uint32_t epoch, 
     const char* sk = ring + slot * kSlotBytes;
     const char* sv = sk + kToks * kPitch;
     slot = slot + 1 == SLOTS ? 0 : slot + 1;
+#if QQ_ATTN_FMA
+    // ---- the same stage with fp32 FMA instead of tensor-core MMA: lane ->
+    // query head gid, channels [32 tig, 32 tig + 32); scores of the 16 rows
+    // summed over the four lanes of a head, softmax per lane (the four
+    // lanes of a head hold the same values), O^T in acc as 32 channels.
+    {
+      float sc[kToks];
+#pragma unroll
+      for (int r = 0; r < kToks; ++r) {
+        const uint4* kr = reinterpret_cast<const uint4*>(sk + r * kPitch + tig * 64);
+        float t = 0.f;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const uint4 w = kr[c4];
+          const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
+          const uint32_t qw[4] = {qb[2 * c4][0], qb[2 * c4][1], qb[2 * c4 + 1][0], qb[2 * c4 + 1][1]};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            t = fmaf(__uint_as_float(kw[e] << 16), __uint_as_float(qw[e] << 16), t);
+            t = fmaf(__uint_as_float(kw[e] & 0xFFFF0000u), __uint_as_float(qw[e] & 0xFFFF0000u), t);
+          }
+        }
+        sc[r] = t;
+      }
+      float mx = kNegInf;
+#pragma unroll
+      for (int r = 0; r < kToks; ++r) {
+        sc[r] += __shfl_xor_sync(0xffffffffu, sc[r], 1);
+        sc[r] += __shfl_xor_sync(0xffffffffu, sc[r], 2);
+        sc[r] = r < ntok ? sc[r] * a.scale_log2 : kNegInf;
+        mx = fmaxf(mx, sc[r]);
+      }
+      const float mn = fmaxf(m_a, mx);
+      const float base = mn == kNegInf ? 0.f : mn;
+      if (mn != m_a) {
+        const float al = fast_exp2(m_a - base);
+        l_a *= al;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          acc[mt][0] *= al;
+          acc[mt][1] *= al;
+          acc[mt][2] *= al;
+          acc[mt][3] *= al;
+        }
+      }
+      m_a = mn;
+#pragma unroll
+      for (int r = 0; r < kToks; ++r) {
+        const float pr = fast_exp2(sc[r] - base);
+        l_a += pr;
+        const uint4* vr = reinterpret_cast<const uint4*>(sv + r * kPitch + tig * 64);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const uint4 w = vr[c4];
+          const uint32_t vw[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float* o = &acc[2 * c4 + (e >> 1)][(e & 1) * 2];
+            o[0] = fmaf(pr, __uint_as_float(vw[e] << 16), o[0]);
+            o[1] = fmaf(pr, __uint_as_float(vw[e] & 0xFFFF0000u), o[1]);
+          }
+        }
+      }
+    }
+#else
     // ---- S^T = K . Q^T
     // two accumulators (even / odd k-steps) halve the dependent MMA chain
     float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
@@ -476,15 +562,18 @@ __device__ __forceinline__ void stream_share(const AttnArgs& a, uint32_t epoch, 
       mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
       mma_bf16_16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
     }
+#endif
     if (!cc.s_last) continue;
 
     // ---- end of this warp's portion of segment (req, head)
     float la = l_a, lb = l_b;
+#if !QQ_ATTN_FMA
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       la += __shfl_xor_sync(0xffffffffu, la, o);
       lb += __shfl_xor_sync(0xffffffffu, lb, o);
     }
+#endif
     const int seg0 = cc.stage_seg_start;
     const int seg1 = seg0 + cc.s_n;
     const int w_first = sp.owner(seg0), w_last = sp.owner(seg1 - 1);
@@ -492,6 +581,12 @@ __device__ __forceinline__ void stream_share(const AttnArgs& a, uint32_t epoch, 
     if (w_first == w_last) {
       // the whole segment is this warp's: normalize and write bf16
       __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)cc.s_req * a.out_stride;
+#if QQ_ATTN_FMA
+      const float inv = 1.f / la;
+      __nv_bfloat16* oh = out + (cc.s_head * kG + gid) * kD + 32 * tig;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) oh[j] = __float2bfloat16_rn(acc[j >> 2][j & 3] * inv);
+#else
       const float inv_a = 1.f / la, inv_b = 1.f / lb;
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
@@ -501,6 +596,7 @@ __device__ __forceinline__ void stream_share(const AttnArgs& a, uint32_t epoch, 
         out[qh_a * kD + d0 + 8] = __float2bfloat16_rn(acc[mt][2] * inv_a);
         out[qh_b * kD + d0 + 8] = __float2bfloat16_rn(acc[mt][3] * inv_b);
       }
+#endif
       continue;
     }
     // split segment: record (m, l, O) in slot 0 (the share's first segment)
@@ -516,6 +612,11 @@ __device__ __forceinline__ void stream_share(const AttnArgs& a, uint32_t epoch, 
       bt.task[t] = SegTask{cc.s_req, cc.s_head, W, min(w_last, W0 + WARPS - 1), ba, bb, rslot, slot_ba, slot_here};
     }
     float* rec = a.part + ((int64_t)W * 2 + rslot) * kPartFloats;
+#if QQ_ATTN_FMA
+#pragma unroll
+    for (int j = 0; j < 32; ++j) rec[gid * kD + 32 * tig + j] = acc[j >> 2][j & 3];
+    if (tig == 0) *reinterpret_cast<float2*>(rec + kG * kD + gid * 2) = make_float2(m_a, la);
+#else
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
       const int d0 = mt * 16 + gid;
@@ -531,6 +632,7 @@ __device__ __forceinline__ void stream_share(const AttnArgs& a, uint32_t epoch, 
       ml[(2 * tig + 1) * 2] = m_b;
       ml[(2 * tig + 1) * 2 + 1] = lb;
     }
+#endif
   }
 }
 
