@@ -28,8 +28,10 @@ layer-step), ``--case prefill`` (one 32K-token prefill's K/V write + Quest
 bounds over 48 layers, fused against the reference's order), ``--case config2`` (16 ragged
 requests up to 131K tokens, Mode 2) and ``--case config3`` (HiSparse, 32
 requests at 65,536 tokens with the host tier, against the host-link
-roofline).  ``--context-limit`` runs config 1 under a larger engine
-``max_context_len``.
+roofline), ``--case config4`` (one GPU's 8-request shard of the end-to-end
+run: the reference ``Engine`` and random-init Qwen3-30B-A3B with the B200
+attention backend; decode tokens/s and the backend's share of it).
+``--context-limit`` runs config 1 under a larger engine ``max_context_len``.
 Multi-GPU: one process per GPU (torchrun); config 1's 64 requests are sharded
 in contiguous blocks over the GPUs (64/N per GPU) with no collective on the
 hot path (strong scaling, the configuration the benchmark names); ``--weak``
@@ -661,6 +663,117 @@ def config0_case(args) -> None:
     }), flush=True)
 
 
+# --------------------------------------------------------------------------- config 4
+
+
+def config4_case(args) -> None:
+    """``--case config4``: end-to-end decode through the reference ``Engine`` on one GPU's shard.
+
+    The benchmark's config 4 is a random-init Qwen3-30B-A3B (48 layers, hidden 2048,
+    32 / 4 heads x 128, 128 experts top-8, moe_intermediate 768, vocab 151936,
+    bf16, weights ~N(0, 0.02)), batch 64 at context 32768, 128 new tokens,
+    quest mode, requests sharded over 8 GPUs with only the attention backend
+    replaced.  Requests are independent, so one GPU's shard (64 / 8 = 8
+    requests) runs here alone: the reference's model and engine (its
+    prefill, batched decode and MoE loop) with ``B200QuestOnlyBackend`` behind
+    ``Engine._make_backend``, the whole integration a user makes.
+    Prompts are seeded uniform-random token ids.  Reported: decode tokens/s of
+    the shard (host-timed around ``Engine._decode``, synchronized), the box's
+    tokens/s as 8 such shards (no collective on the path), prefill seconds,
+    and the attention backend's share of the decode time (CUDA events around
+    every ``forward_decode``).  The weights are drawn on the GPU with a
+    seeded generator (the reference's ``init_random_weights`` draws 30.5 B
+    values on the host; same distribution).
+    """
+    from qwenquest import Engine, EngineConfig, Qwen3MoeForCausalLM
+    from qwenquest.config import Qwen3MoeConfig, parse_hisparse_config
+
+    from qwenquest_b200 import B200QuestOnlyBackend
+
+    class B200Engine(Engine):
+        def _make_backend(self):
+            sparse = parse_hisparse_config({"algorithm": "quest", "top_k": TOP_K, "quest_page_size": PAGE})
+            return B200QuestOnlyBackend(self.req_to_token_pool, self.token_to_kv_pool, sparse)
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_req, ctx, new = args.c4_requests, args.c4_context, args.c4_new_tokens
+    t0 = time.perf_counter()
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = Qwen3MoeForCausalLM(Qwen3MoeConfig())
+    finally:
+        torch.set_default_dtype(prev)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    with torch.no_grad():
+        for name, param in model.named_parameters():
+            if name.endswith("norm.weight"):
+                param.fill_(1.0)
+            else:
+                param.normal_(0.0, 0.02, generator=gen)
+    model.eval()
+    n_params = sum(p.numel() for p in model.parameters())
+    engine = B200Engine(model, EngineConfig(attention_mode="quest", max_running_requests=n_req,
+                                            max_context_len=ctx + new + 1))
+    init_s = time.perf_counter() - t0
+    g = torch.Generator().manual_seed(args.seed + 1)
+    prompts = [torch.randint(0, model.config.vocab_size, (ctx,), generator=g).tolist() for _ in range(n_req)]
+
+    phase = {"prefill": 0.0, "decode": 0.0, "decode_steps": 0}
+    orig_prefill, orig_decode = engine._prefill, engine._decode
+
+    def timed_phase(fn, key):
+        def run(*a, **k):
+            torch.cuda.synchronize(dev)
+            t = time.perf_counter()
+            out = fn(*a, **k)
+            torch.cuda.synchronize(dev)
+            phase[key] += time.perf_counter() - t
+            if key == "decode":
+                phase["decode_steps"] += 1
+            return out
+        return run
+
+    engine._prefill = timed_phase(orig_prefill, "prefill")
+    engine._decode = timed_phase(orig_decode, "decode")
+    backend = engine.attn_backend
+    orig_fd = backend.forward_decode
+    events = []
+
+    def fd(q, k, v, layer, batch):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = orig_fd(q, k, v, layer, batch)
+        e1.record()
+        events.append((e0, e1))
+        return out
+
+    backend.forward_decode = fd
+    outs = engine.generate(prompts, max_new_tokens=new, stop_token_ids=[])
+    torch.cuda.synchronize(dev)
+    backend.check_errors()
+    attn_s = sum(a.elapsed_time(b) for a, b in events) / 1e3
+    tokens = sum(len(o.output_ids) for o in outs)
+    decode_tokens = tokens - n_req  # the first token of each request comes from its prefill
+    dec_tps = decode_tokens / phase["decode"]
+    print(json.dumps({
+        "case": "config4", "metric": "end-to-end decode tokens/s (reference Engine, B200 attention backend)",
+        "value": dec_tps, "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0, 0.02) drawn on the GPU, seeded uniform-random prompt ids)",
+        "config": {"workload": f"config4 shard: {n_req} requests x {ctx}-token prompts, {new} new tokens, "
+                               "random-init Qwen3-30B-A3B (48 layers, 128 experts top-8), quest mode "
+                               "(top_k 2048 / page 64), the reference Engine with B200QuestOnlyBackend",
+                   "params": n_params, "shard_of": 64},
+        "box_tokens_per_s_8_shards": 8 * dec_tps,
+        "decode_s": phase["decode"], "decode_steps": phase["decode_steps"], "prefill_s": phase["prefill"],
+        "prefill_tokens_per_s": n_req * ctx / phase["prefill"],
+        "attention_decode_s": attn_s, "attention_share_of_decode": attn_s / phase["decode"],
+        "init_s": init_s, "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9,
+    }), flush=True)
+
+
 def qkv_steps(qkv, total):
     """The same per-layer inputs for every step ([steps, layers, ...] views)."""
     return tuple(t.unsqueeze(0).expand(total, *t.shape) for t in qkv)
@@ -855,9 +968,14 @@ def main() -> None:
     ap.add_argument("--resident", type=int, default=RESIDENT, help="physical KV buffers")
     ap.add_argument("--context-limit", type=int, default=None,
                     help="engine max_context_len above the requests' lengths (profiling cases only)")
-    ap.add_argument("--case", choices=["decode", "prefill", "config0", "config2", "config3"], default="decode",
+    ap.add_argument("--case", choices=["decode", "prefill", "config0", "config2", "config3", "config4"],
+                    default="decode",
                     help="decode: the benchmark, config 1 (default); prefill: the prefill K/V write + bounds; "
-                         "config2 / config3: the ragged and HiSparse benchmark configs (1 GPU each)")
+                         "config2 / config3: the ragged and HiSparse benchmark configs (1 GPU each); "
+                         "config4: end-to-end decode through the reference Engine, one GPU's shard")
+    ap.add_argument("--c4-requests", type=int, default=8, help="config4: requests of the shard (64 / 8 GPUs)")
+    ap.add_argument("--c4-context", type=int, default=32768, help="config4: prompt tokens per request")
+    ap.add_argument("--c4-new-tokens", type=int, default=128, help="config4: tokens generated per request")
     ap.add_argument("--path", choices=["graph", "eager"], default="graph",
                     help="headline path: the decode step replayed as a CUDA graph (default) or the eager calls")
     ap.add_argument("--weak", action="store_true",
@@ -867,7 +985,7 @@ def main() -> None:
     if args.case != "decode":
         if int(os.environ.get("RANK", "0")) == 0:
             {"prefill": prefill_case, "config0": config0_case, "config2": config2_case,
-             "config3": config3_case}[args.case](args)
+             "config3": config3_case, "config4": config4_case}[args.case](args)
         return
     from qwenquest_b200.graphs import DecodeStepGraph
     from qwenquest_b200.sharding import max_over_ranks, shard_requests
