@@ -30,7 +30,9 @@ requests up to 131K tokens, Mode 2) and ``--case config3`` (HiSparse, 32
 requests at 65,536 tokens with the host tier, against the host-link
 roofline), ``--case config4`` (one GPU's 8-request shard of the end-to-end
 run: the reference ``Engine`` and random-init Qwen3-30B-A3B with the B200
-attention backend; decode tokens/s and the backend's share of it).
+attention backend; decode tokens/s and the backend's share of it),
+``--case prefill_attn`` (the dense causal prefill attention of one 32K-token
+request on the tensor cores, TFLOP/s against the reference's gather + SDPA).
 ``--context-limit`` runs config 1 under a larger engine ``max_context_len``.
 Multi-GPU: one process per GPU (torchrun); config 1's 64 requests are sharded
 in contiguous blocks over the GPUs (64/N per GPU) with no collective on the
@@ -340,6 +342,117 @@ def prefill_case(args) -> None:
         "gpu_launches": n_layers * args.steps,
         "roofline": {"bound": "hbm", "kernel": "extend_kv", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "algorithmic_bytes_per_launch": per_launch, "peak_kind": peak_kind},
+        "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def prefill_attn_case(args) -> None:
+    """``--case prefill_attn``: dense causal prefill attention of one ``--prefill-tokens``-token
+    request (config 4's prompt, 32 768 by default), 32 query / 4 KV heads x 128, bf16.
+
+    B200: one ``qq_extend_attention`` launch (tcgen05, K/V rows read in place
+    through ``req_to_token``).  Reference: its own ``forward_extend`` loop body
+    (``attention/base.py:78-93``) on the same GPU: ``k_buf[locs]`` /
+    ``v_buf[locs]`` gathers, then ``extend_attention`` (``ops.py:18-45``:
+    ``repeat_interleave`` and torch SDPA with ``is_causal``).  FLOPs: 4 x H x D
+    per visible (query, key) pair.  Pool rows in a seeded random order.
+    """
+    from qwenquest.attention.ops import extend_attention as ref_extend
+
+    from qwenquest_b200 import _lib
+    from qwenquest_b200.hisparse import host_device_pointer
+    from qwenquest_b200.kernels import extend_tiles
+    from qwenquest_b200.quest import stream_of
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n = args.prefill_tokens
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    rows = n + 1
+    k = torch.randn((rows, KV, D), generator=gen, device=dev).to(torch.bfloat16)
+    v = torch.randn((rows, KV, D), generator=gen, device=dev).to(torch.bfloat16)
+    qs = [torch.randn((n, H, D), generator=gen, device=dev).to(torch.bfloat16) for _ in range(2)]
+    r2t = (torch.randperm(n, generator=gen, device=dev) + 1).to(torch.int32)[None].contiguous()
+    scaling = D ** -0.5
+    lib = _lib.load()
+    i64 = dict(dtype=torch.int64, device=dev)
+    arrays = [torch.zeros(1, **i64), torch.full((1,), n, **i64), torch.zeros(1, **i64), torch.zeros(1, **i64)]
+    batch = _lib.QQExtendBatch(arrays[0].data_ptr(), arrays[1].data_ptr(), arrays[2].data_ptr(),
+                               arrays[3].data_ptr(), 0, n, 1, n)
+    table = _lib.QQTokenTable(r2t.data_ptr(), r2t.stride(0), 1)
+    tiles = torch.tensor(extend_tiles([n], [0]), dtype=torch.int32, device=dev)
+    out = torch.empty((n, H * D), dtype=torch.bfloat16, device=dev)
+    err = torch.zeros(1, dtype=torch.int32).pin_memory()
+    err_dev = host_device_pointer(err)
+    stream = stream_of(dev)
+    step = [0]
+
+    def ours():
+        q = qs[step[0] % 2]
+        step[0] += 1
+        rc = lib.qq_extend_attention(batch, table, tiles.data_ptr(), tiles.numel(), q.data_ptr(), _lib.QQ_BF16, H,
+                                     KV, D, q.stride(0), k.data_ptr(), v.data_ptr(), k.stride(0), rows, scaling,
+                                     out.data_ptr(), out.stride(0), err_dev, stream)
+        _lib.check(rc, "extend attention")
+
+    locs = r2t[0].long()
+
+    def reference():
+        q = qs[step[0] % 2]
+        step[0] += 1
+        return ref_extend(q, k[locs], v[locs], prefix_len=0, scaling=scaling)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / args.steps
+
+    clocks = ClockSampler(0)
+    clocks.start()
+    time.sleep(0.3)
+    ref_ms = timed(reference)
+    ms = timed(ours)
+    clock_info = clocks.stop()
+    torch.cuda.synchronize(dev)
+    _lib.raise_device_error(int(err[0]), "(extend attention)")
+    step[0] = 0
+    ref_out = reference()
+    step[0] = 0
+    ours()
+    torch.cuda.synchronize(dev)
+    a_, b_ = out.float(), ref_out.float()
+    step_ = torch.exp2(torch.floor(torch.log2(b_.abs().clamp_min(1e-30))) - 7)
+    within = bool(((a_ - b_).abs() <= torch.clamp(step_, min=2e-2)).all())
+    flops = 4.0 * H * D * n * (n + 1) / 2
+    achieved = flops / (ms / 1e3) / 1e12
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        peak, peak_kind = float(peaks["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
+    except (OSError, KeyError, ValueError):
+        peak, peak_kind = 1590.0, "fallback"
+    line = {
+        "case": "prefill_attn", "metric": "dense causal prefill attention, TFLOP/s (causal FLOPs)",
+        "value": achieved, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": f"one {n}-token prefill, 1 layer, 32 query / 4 KV heads x 128, bf16, "
+                               "pool rows in a seeded random order",
+                   "l2": f"Q ({n * H * D * 2 / 1e6:.0f} MB per step, two inputs alternating) larger than L2"},
+        "tokens_per_s": n / (ms / 1e3),
+        "reference": {"ms_per_step": ref_ms, "value": flops / (ref_ms / 1e3) / 1e12,
+                      "path": "k_buf[locs], v_buf[locs], repeat_interleave, torch SDPA (is_causal)"},
+        "speedup_vs_reference": ref_ms / ms,
+        "within_tolerance_of_reference": within,
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "tensor", "kernel": "prefill_attn", "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": peak_kind},
         "clocks": clock_info,
     }
     print(json.dumps(line), flush=True)
@@ -968,11 +1081,14 @@ def main() -> None:
     ap.add_argument("--resident", type=int, default=RESIDENT, help="physical KV buffers")
     ap.add_argument("--context-limit", type=int, default=None,
                     help="engine max_context_len above the requests' lengths (profiling cases only)")
-    ap.add_argument("--case", choices=["decode", "prefill", "config0", "config2", "config3", "config4"],
+    ap.add_argument("--case", choices=["decode", "prefill", "prefill_attn", "config0", "config2", "config3",
+                                       "config4"],
                     default="decode",
                     help="decode: the benchmark, config 1 (default); prefill: the prefill K/V write + bounds; "
                          "config2 / config3: the ragged and HiSparse benchmark configs (1 GPU each); "
-                         "config4: end-to-end decode through the reference Engine, one GPU's shard")
+                         "config4: end-to-end decode through the reference Engine, one GPU's shard; "
+                         "prefill_attn: the dense causal prefill attention against the reference's")
+    ap.add_argument("--prefill-tokens", type=int, default=PREFIX, help="prefill_attn: tokens of the request")
     ap.add_argument("--c4-requests", type=int, default=8, help="config4: requests of the shard (64 / 8 GPUs)")
     ap.add_argument("--c4-context", type=int, default=32768, help="config4: prompt tokens per request")
     ap.add_argument("--c4-new-tokens", type=int, default=128, help="config4: tokens generated per request")
@@ -984,7 +1100,7 @@ def main() -> None:
     args.warmup = max(args.warmup, 3)
     if args.case != "decode":
         if int(os.environ.get("RANK", "0")) == 0:
-            {"prefill": prefill_case, "config0": config0_case, "config2": config2_case,
+            {"prefill": prefill_case, "prefill_attn": prefill_attn_case, "config0": config0_case, "config2": config2_case,
              "config3": config3_case, "config4": config4_case}[args.case](args)
         return
     from qwenquest_b200.graphs import DecodeStepGraph

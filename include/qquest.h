@@ -199,6 +199,30 @@ int qq_quest_extend_kv(const qq_quest_state* st, int layer, int write_counters,
                        void* v_pool, int64_t pool_row_stride, int64_t pool_rows, const qq_hot_buffer* hot,
                        uint32_t* err, void* stream);
 
+/* ---- dense causal prefill attention (tcgen05) ------------------------- */
+/* For every request i of an extend batch: out[token_offsets[i] + t] (t <
+ * seq_lens[i] - prefix_lens[i]) = causal attention of q[token_offsets[i] + t]
+ * (position prefix_lens[i] + t, q_heads x head_dim) over the keys and values
+ * of positions 0 .. prefix_lens[i] + t, read in place from k_pool / v_pool
+ * at rows table->req_to_token[req][pos]; query head h reads KV head
+ * h / (q_heads / kv_heads); fp32 scores, softmax and accumulation, bf16
+ * result.  tiles (device int32 [num_tiles]) lists the work as
+ * (batch entry << 16) | t-tile (128 new tokens each), one entry per tile of
+ * every request, heaviest first (qwenquest_b200.kernels.extend_tiles builds
+ * it); each tile runs on one CTA per pair of query heads.  bf16, head_dim
+ * 128, an even number of query heads per KV head, 16-byte aligned rows and
+ * pointers, num_tiles <= 65535; anything else returns QQ_ERR_UNSUPPORTED.
+ * Rows outside [0, num_rows) are read as row 0 and a batch entry whose
+ * lengths do not fit the table or the token count is skipped, both reported
+ * as QQ_DEV_ERR_BOUNDS in err (nullable).  Replaces the per-request loop of
+ * AttentionBackend.forward_extend (attention/base.py:71-93) over
+ * extend_attention (attention/ops.py:18-45). */
+int qq_extend_attention(const qq_extend_batch* batch, const qq_token_table* table, const int32_t* tiles,
+                        int num_tiles, const void* q, int dtype, int q_heads, int kv_heads, int head_dim,
+                        int64_t q_stride, const void* k_pool, const void* v_pool, int64_t kv_row_stride,
+                        int64_t num_rows, float scaling, void* out, int64_t out_stride, uint32_t* err,
+                        void* stream);
+
 /* ---- [Q3] per-step bounds fold + finalize ----------------------------- */
 #define QQ_STEP_FOLD 1     /* running min/max <- key of the previous token */
 #define QQ_STEP_FINALIZE 2 /* finalize pages whose 64th token arrived, advance counters */

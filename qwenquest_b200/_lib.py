@@ -142,6 +142,9 @@ SIGNATURES: dict[str, tuple] = {
     "qq_quest_extend_kv": (
         c_int, [_S, c_int, c_int, _E, _T, c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p,
                 c_int64, c_int64, _HB, c_void_p, c_void_p]),
+    "qq_extend_attention": (
+        c_int, [_E, _T, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p, c_void_p,
+                c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
     "qq_quest_decode_step": (
         c_int, [_S, c_int, c_int, c_int, _PP, c_int, c_int64, _B, c_void_p, c_void_p, _T, c_int64,
                 c_void_p, c_size_t, c_void_p]),

@@ -37,6 +37,7 @@ from qwenquest.config import parse_hisparse_config
 from qwenquest_b200 import _lib
 from qwenquest_b200._lib import QQ_STEP_FINALIZE, QQ_STEP_FOLD, check
 from qwenquest_b200.hisparse import HiSparseCoordinator, _DeviceError
+from qwenquest_b200.kernels import EXTEND_TILE, extend_tiles
 from qwenquest_b200.quest import QuestAlgorithm, dtype_code, stream_of
 
 __all__ = ["B200QuestHiSparseBackend", "B200QuestOnlyBackend"]
@@ -60,8 +61,21 @@ class _ExtendPlan:
     reqs_dev: torch.Tensor  # device int64 [bs]
     tensors: tuple  # every device tensor the struct points into (kept alive with it)
     qq: _lib.QQExtendBatch
+    prefix: list[int] = None
     unfused: bool = False
     admission: object = None
+    tiles: torch.Tensor | None = None
+
+    @property
+    def num_tiles(self) -> int:
+        return sum(-(-(s - p) // EXTEND_TILE) for s, p in zip(self.seq_lens, self.prefix, strict=True))
+
+    def tiles_dev(self) -> torch.Tensor:
+        """The tile list of ``qq_extend_attention`` (heaviest first), built once per batch."""
+        if self.tiles is None:
+            self.tiles = torch.tensor(extend_tiles(self.seq_lens, self.prefix), dtype=torch.int32,
+                                      device=self.reqs_dev.device)
+        return self.tiles
 
 
 class _QuestDecodeMixin:
@@ -72,8 +86,14 @@ class _QuestDecodeMixin:
 
     def _extend_attention(self, q, layer, batch) -> torch.Tensor:
         """The attention half of the reference's ``forward_extend`` (``base.py:71-93``), over the K/V rows
-        already in the pool: dense causal prefill through the reference's own ``extend_attention``."""
+        already in the pool.  bf16 pools of head_dim 128 with an even number of query heads per KV head:
+        one ``qq_extend_attention`` launch for the whole batch (tcgen05 tensor cores, rows read in place
+        through ``req_to_token``).  Other geometries (the reference's fp32 test models) keep the
+        reference's own per-request ``extend_attention`` loop on the GPU."""
         k_buf, v_buf = self.token_to_kv_pool.get_kv_buffer(layer.layer_id)
+        plan = self._extend_plan(batch)
+        if self._prefill_kernel_fits(q, k_buf, plan):
+            return self._extend_attention_kernel(q, k_buf, v_buf, layer, plan)
         offsets = batch.extend_token_offsets()
         outputs = []
         for i in range(batch.batch_size):
@@ -82,6 +102,31 @@ class _QuestDecodeMixin:
             outputs.append(extend_attention(q[offsets[i]:offsets[i + 1]], k_buf[locs], v_buf[locs],
                                             prefix_len=int(batch.extend_prefix_lens[i]), scaling=layer.scaling))
         return torch.cat(outputs, dim=0)
+
+    def _prefill_kernel_fits(self, q, k_buf, plan) -> bool:
+        if not self.fused_prefill_attention or q.dim() != 3 or k_buf.dim() != 3:
+            return False
+        heads, dim = q.shape[1], q.shape[2]
+        kv = k_buf.shape[1]
+        return (q.dtype == torch.bfloat16 and k_buf.dtype == torch.bfloat16 and dim == 128
+                and k_buf.shape[2] == dim and heads % kv == 0 and (heads // kv) % 2 == 0
+                and k_buf.stride(2) == 1 and k_buf.stride(1) == dim and (k_buf.stride(0) * 2) % 16 == 0
+                and k_buf.data_ptr() % 16 == 0 and plan.num_tiles <= 65535 and len(plan.reqs) < 32768)
+
+    def _extend_attention_kernel(self, q, k_buf, v_buf, layer, plan) -> torch.Tensor:
+        tokens, heads, dim = q.shape
+        if q.stride(2) != 1 or q.stride(1) != dim or (q.stride(0) * 2) % 16 or q.data_ptr() % 16:
+            q = q.contiguous()
+        out = torch.empty((tokens, heads * dim), dtype=q.dtype, device=self.device)
+        tiles = plan.tiles_dev()
+        rc = self.lib.qq_extend_attention(
+            plan.qq, self._token_table(), tiles.data_ptr(), tiles.numel(), q.data_ptr(), dtype_code(q.dtype),
+            heads, k_buf.shape[1], dim, q.stride(0), k_buf.data_ptr(), v_buf.data_ptr(), k_buf.stride(0),
+            k_buf.shape[0], float(layer.scaling), out.data_ptr(), out.stride(0), self._xerr.ptr(),
+            stream_of(self.device),
+        )
+        check(rc, "prefill attention")
+        return out
 
     def _setup_decode(self, max_reqs: int) -> None:
         dev = self.device
@@ -109,6 +154,9 @@ class _QuestDecodeMixin:
         #: layer (qq_quest_extend_kv); False keeps the reference's order:
         #: set_kv_buffer per layer, bounds from the pool after the last layer
         self.fused_extend = True
+        #: dense prefill attention as one qq_extend_attention launch per layer
+        #: (bf16, head_dim 128); False keeps the reference's per-request loop
+        self.fused_prefill_attention = True
         self._xplan: _ExtendPlan | None = None
         self._xerr = _DeviceError(torch.zeros(1, dtype=torch.int32).pin_memory())
 
@@ -147,7 +195,7 @@ class _QuestDecodeMixin:
     def check_errors(self) -> None:
         """Raise for device errors reported by earlier launches (no synchronisation)."""
         _lib.raise_device_error(self._attn_err.take(), "(attention)")
-        _lib.raise_device_error(self._xerr.take(), "(prefill K/V write)")
+        _lib.raise_device_error(self._xerr.take(), "(prefill K/V write or attention)")
 
     # ----------------------------------------------------------------- prefill
 
@@ -180,7 +228,8 @@ class _QuestDecodeMixin:
             raise ValueError(f"extend batch: {loc.numel()} out_cache_loc rows for {sum(new_h)} new tokens")
         qq = _lib.QQExtendBatch(reqs.data_ptr(), seq.data_ptr(), prefix.data_ptr(), offsets.data_ptr(),
                                 loc.data_ptr(), loc.numel(), len(seq_h), max(seq_h, default=0))
-        plan = _ExtendPlan(batch, [int(x) for x in reqs.tolist()], seq_h, reqs, (reqs, seq, prefix, offsets, loc), qq)
+        plan = _ExtendPlan(batch, [int(x) for x in reqs.tolist()], seq_h, reqs, (reqs, seq, prefix, offsets, loc), qq,
+                           prefix=[int(x) for x in prefix.tolist()])
         self._xplan = plan
         return plan
 

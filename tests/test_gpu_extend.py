@@ -8,8 +8,11 @@ stream).  With ``fused_extend = False`` it follows the reference:
 last layer (``quest_only.py:101-128``) or, in Mode 3, the admission copies in
 ``on_extend_finished`` (``coordinator.py:138-174``).  Both must leave
 bit-identical pools, bounds, running bounds, counters, skip flags, hot
-buffers, host tiers and slot layouts, and give bit-identical prefill outputs;
-the bounds must also equal the numpy oracle's, computed from the pool's keys.
+buffers, host tiers and slot layouts, and give the same prefill outputs:
+bit-identical where both take the reference's ``extend_attention``, within
+max(2e-2, one bf16 step) where the fused backend's dense prefill attention is
+the tcgen05 kernel (bf16, head_dim 128) and the other is torch SDPA; the
+bounds must also equal the numpy oracle's, computed from the pool's keys.
 
 Cases: ragged lengths (1 token, below / at / above a page, several pages),
 a chunked prefill whose cached prefix ends inside a page, layers outside the
@@ -95,6 +98,18 @@ class _Run:
         return outs
 
 
+def _assert_same_outputs(outs_a, outs_b, dtype, d) -> None:
+    """Prefill outputs of the fused and the reference-order backend (layer by layer)."""
+    kernel = dtype == torch.bfloat16 and d == 128  # qq_extend_attention on the fused side
+    for oa, ob in zip(outs_a, outs_b, strict=True):
+        if not kernel:
+            assert torch.equal(oa, ob)
+            continue
+        a, b = oa.float(), ob.float()
+        step = torch.exp2(torch.floor(torch.log2(b.abs().clamp_min(1e-30))) - 7)
+        assert bool(((a - b).abs() <= torch.clamp(step, min=2e-2)).all()), float((a - b).abs().max())
+
+
 def _assert_same_state(a: _Run, b: _Run) -> None:
     for li in range(LAYERS):
         assert torch.equal(a.pool.k_buffer[li], b.pool.k_buffer[li]), li
@@ -131,15 +146,13 @@ def test_quest_extend_fused_equals_reference_order(dtype, kv, d, cuda_device):
     # first prefill: ragged, no prefix
     reqs1, new1 = [0, 1, 2, 3, 4, 5], [1, 15, 16, 17, 100, 333]
     outs = [r.extend(reqs1, [0] * 6, new1) for r in runs]
-    for oa, ob in zip(*outs, strict=True):
-        assert torch.equal(oa, ob)
+    _assert_same_outputs(*outs, dtype, d)
     _assert_same_state(*runs)
     _assert_oracle_bounds(runs[0], reqs1, new1)
     # second prefill: two requests continue after a prefix ending inside a page, one new request
     reqs2, prefix2, new2 = [3, 4, 6], [17, 100, 0], [40, 7, 64]
     outs = [r.extend(reqs2, prefix2, new2) for r in runs]
-    for oa, ob in zip(*outs, strict=True):
-        assert torch.equal(oa, ob)
+    _assert_same_outputs(*outs, dtype, d)
     torch.cuda.synchronize(cuda_device)
     for r in runs:
         r.be.check_errors()
@@ -157,8 +170,7 @@ def test_hisparse_admission_fused_equals_reference_order(dtype, kv, d, cuda_devi
     # lengths below, at and above the hot buffer (128 slots)
     reqs, new = [0, 1, 2, 3], [5, 128, 129, 300]
     outs = [r.extend(reqs, [0] * 4, new) for r in runs]
-    for oa, ob in zip(*outs, strict=True):
-        assert torch.equal(oa, ob)
+    _assert_same_outputs(*outs, dtype, d)
     torch.cuda.synchronize(cuda_device)
     for r in runs:
         r.be.check_errors()
@@ -190,8 +202,7 @@ def test_quest_extend_large_batch(cuda_device):
     runs = [_Run("quest", torch.bfloat16, 4, 128, fused, cuda_device, seed=3) for fused in (True, False)]
     reqs, new = list(range(MAX_REQS)), [1000, 999, 1001 - 64, 640, 1017, 1008, 961, 1023]
     outs = [r.extend(reqs, [0] * MAX_REQS, new) for r in runs]
-    for oa, ob in zip(*outs, strict=True):
-        assert torch.equal(oa, ob)
+    _assert_same_outputs(*outs, torch.bfloat16, 128)
     torch.cuda.synchronize(cuda_device)
     for r in runs:
         r.be.check_errors()
