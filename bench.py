@@ -32,7 +32,9 @@ roofline), ``--case config4`` (one GPU's 8-request shard of the end-to-end
 run: the reference ``Engine`` and random-init Qwen3-30B-A3B with the B200
 attention backend; decode tokens/s and the backend's share of it),
 ``--case prefill_attn`` (the dense causal prefill attention of one 32K-token
-request on the tensor cores, TFLOP/s against the reference's gather + SDPA).
+request on the tensor cores, TFLOP/s against the reference's gather + SDPA),
+``--case moe`` (one Qwen3-30B-A3B MoE block at 8 decode tokens and a 32K-token
+prefill, against the reference's per-expert loop).
 ``--context-limit`` runs config 1 under a larger engine ``max_context_len``.
 Multi-GPU: one process per GPU (torchrun); config 1's 64 requests are sharded
 in contiguous blocks over the GPUs (64/N per GPU) with no collective on the
@@ -458,6 +460,92 @@ def prefill_attn_case(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def moe_case(args) -> None:
+    """``--case moe``: one Qwen3-30B-A3B MoE block (hidden 2048, 128 experts of 768, top 8,
+    bf16, weights N(0, 0.02)) at config 4's decode batch of one GPU (``--moe-tokens``,
+    8) and a 32K-token prefill.
+
+    B200: ``B200SparseMoeBlock`` (the reference's routing, then ``qq_moe_experts``:
+    two tcgen05 grouped GEMMs and the combine).  Reference: its own
+    ``Qwen3MoeSparseMoeBlock.forward`` (per-expert loop) on the same GPU.
+    Decode is bound by the distinct experts' weight bytes (HBM); prefill by
+    the FLOPs (6 x pairs x hidden x intermediate).
+    """
+    from qwenquest.config import Qwen3MoeConfig
+    from qwenquest.model.qwen3_moe import Qwen3MoeSparseMoeBlock
+
+    from qwenquest_b200.moe import B200SparseMoeBlock
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = Qwen3MoeConfig()
+    with torch.device(dev):
+        blk = Qwen3MoeSparseMoeBlock(cfg).to(torch.bfloat16)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    with torch.no_grad():
+        for p_ in blk.parameters():
+            p_.copy_(torch.randn(p_.shape, generator=gen, device=dev) * 0.02)
+    ours = B200SparseMoeBlock(blk)
+    hidden, inter, k = cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts_per_tok
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        tflops_peak, hbm_peak, kind = float(peaks["bf16_tflops"]), float(peaks["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        tflops_peak, hbm_peak, kind = 1590.0, 6650.0, "fallback"
+
+    def timed(fn, x, steps):
+        for _ in range(args.warmup):
+            fn(x)
+        torch.cuda.synchronize(dev)
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        for _ in range(steps):
+            fn(x)
+        b_.record()
+        torch.cuda.synchronize(dev)
+        return a_.elapsed_time(b_) / steps
+
+    results = {}
+    clocks = ClockSampler(0)
+    clocks.start()
+    time.sleep(0.3)
+    with torch.no_grad():
+        for name, tokens in (("decode", args.moe_tokens), ("prefill", args.moe_prefill_tokens)):
+            x = (torch.randn((tokens, hidden), generator=gen, device=dev)).to(torch.bfloat16)
+            steps = args.steps if name == "decode" else max(2, args.steps // 10)
+            ref_ms = timed(blk, x, steps)
+            ms = timed(ours, x, steps)
+            out, ref = ours(x), blk(x)
+            ours.check_errors()
+            tol = 2 * 2.0 ** -8 * float(ref.abs().max())
+            within = float((out.float() - ref.float()).abs().max()) <= tol
+            experts = torch.topk(torch.softmax(blk.gate(x).float(), -1), k, dim=-1).indices
+            active = int(torch.unique(experts).numel())
+            wbytes = active * 3 * hidden * inter * 2
+            flops = 6.0 * tokens * k * hidden * inter
+            results[name] = {"tokens": tokens, "ms": ms, "reference_ms": ref_ms, "speedup_vs_reference": ref_ms / ms,
+                             "active_experts": active, "weight_gb_s": wbytes / (ms / 1e3) / 1e9,
+                             "tflops": flops / (ms / 1e3) / 1e12, "within_tolerance_of_reference": within}
+            del x
+    clock_info = clocks.stop()
+    dec, pre = results["decode"], results["prefill"]
+    line = {
+        "case": "moe", "metric": "Qwen3-MoE block, decode us per layer (8 tokens)", "value": dec["ms"] * 1e3,
+        "unit": "us/layer", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dec["ms"],
+        "higher_is_better": False, "dtype": "bf16", "data": "synthetic (seeded N(0, 0.02) weights, N(0,1) tokens)",
+        "config": {"workload": "Qwen3-30B-A3B MoE block: hidden 2048, 128 experts x 768, top 8, bf16",
+                   "decode_tokens": dec["tokens"], "prefill_tokens": pre["tokens"]},
+        "decode": dec, "prefill": pre,
+        "gpu_launches": 3 * args.steps,
+        "roofline": {"decode": {"bound": "hbm", "achieved": dec["weight_gb_s"], "peak": hbm_peak, "unit": "GB/s",
+                                "frac": dec["weight_gb_s"] / hbm_peak, "peak_kind": kind},
+                     "prefill": {"bound": "tensor", "achieved": pre["tflops"], "peak": tflops_peak,
+                                 "unit": "TFLOP/s", "frac": pre["tflops"] / tflops_peak, "peak_kind": kind}},
+        "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- configs 2 and 3
 
 
@@ -828,6 +916,11 @@ def config4_case(args) -> None:
                 param.normal_(0.0, 0.02, generator=gen)
     model.eval()
     n_params = sum(p.numel() for p in model.parameters())
+    moe_blocks = 0
+    if args.c4_moe:
+        from qwenquest_b200.moe import install_moe
+
+        moe_blocks = install_moe(model)
     engine = B200Engine(model, EngineConfig(attention_mode="quest", max_running_requests=n_req,
                                             max_context_len=ctx + new + 1))
     init_s = time.perf_counter() - t0
@@ -871,8 +964,10 @@ def config4_case(args) -> None:
     tokens = sum(len(o.output_ids) for o in outs)
     decode_tokens = tokens - n_req  # the first token of each request comes from its prefill
     dec_tps = decode_tokens / phase["decode"]
+    replaced = "the attention backend and the MoE blocks" if moe_blocks else "the attention backend only"
     print(json.dumps({
         "case": "config4", "metric": "end-to-end decode tokens/s (reference Engine, B200 attention backend)",
+        "replaced": replaced, "moe_blocks_replaced": moe_blocks,
         "value": dec_tps, "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
         "data": "synthetic (random-init weights N(0, 0.02) drawn on the GPU, seeded uniform-random prompt ids)",
         "config": {"workload": f"config4 shard: {n_req} requests x {ctx}-token prompts, {new} new tokens, "
@@ -1081,7 +1176,7 @@ def main() -> None:
     ap.add_argument("--resident", type=int, default=RESIDENT, help="physical KV buffers")
     ap.add_argument("--context-limit", type=int, default=None,
                     help="engine max_context_len above the requests' lengths (profiling cases only)")
-    ap.add_argument("--case", choices=["decode", "prefill", "prefill_attn", "config0", "config2", "config3",
+    ap.add_argument("--case", choices=["decode", "prefill", "prefill_attn", "moe", "config0", "config2", "config3",
                                        "config4"],
                     default="decode",
                     help="decode: the benchmark, config 1 (default); prefill: the prefill K/V write + bounds; "
@@ -1089,9 +1184,14 @@ def main() -> None:
                          "config4: end-to-end decode through the reference Engine, one GPU's shard; "
                          "prefill_attn: the dense causal prefill attention against the reference's")
     ap.add_argument("--prefill-tokens", type=int, default=PREFIX, help="prefill_attn: tokens of the request")
+    ap.add_argument("--moe-tokens", type=int, default=8, help="moe: tokens of the decode batch (64 / 8 GPUs)")
+    ap.add_argument("--moe-prefill-tokens", type=int, default=PREFIX, help="moe: tokens of the prefill batch")
     ap.add_argument("--c4-requests", type=int, default=8, help="config4: requests of the shard (64 / 8 GPUs)")
     ap.add_argument("--c4-context", type=int, default=32768, help="config4: prompt tokens per request")
     ap.add_argument("--c4-new-tokens", type=int, default=128, help="config4: tokens generated per request")
+    ap.add_argument("--c4-moe", action="store_true",
+                    help="config4: also replace the model's MoE blocks by B200SparseMoeBlock (the benchmark's "
+                         "config replaces the attention backend only)")
     ap.add_argument("--path", choices=["graph", "eager"], default="graph",
                     help="headline path: the decode step replayed as a CUDA graph (default) or the eager calls")
     ap.add_argument("--weak", action="store_true",
@@ -1100,7 +1200,7 @@ def main() -> None:
     args.warmup = max(args.warmup, 3)
     if args.case != "decode":
         if int(os.environ.get("RANK", "0")) == 0:
-            {"prefill": prefill_case, "prefill_attn": prefill_attn_case, "config0": config0_case, "config2": config2_case,
+            {"prefill": prefill_case, "prefill_attn": prefill_attn_case, "moe": moe_case, "config0": config0_case, "config2": config2_case,
              "config3": config3_case, "config4": config4_case}[args.case](args)
         return
     from qwenquest_b200.graphs import DecodeStepGraph

@@ -223,6 +223,43 @@ int qq_extend_attention(const qq_extend_batch* batch, const qq_token_table* tabl
                         int64_t num_rows, float scaling, void* out, int64_t out_stride, uint32_t* err,
                         void* stream);
 
+/* ---- Qwen3-MoE expert block (tcgen05) ---------------------------------- */
+/* The routing of a token batch as (token, slot) pairs grouped by expert:
+ * pairs [expert_offsets[e], expert_offsets[e + 1]) belong to expert e, their
+ * tokens ascending (the order torch.where gives the reference's loop);
+ * pair_weight is each pair's routing weight in bf16; token_pairs[t][s] is the
+ * pair of token t's slot s. */
+typedef struct qq_moe_plan {
+  const int32_t* pair_token;     /* device [num_pairs] */
+  const int64_t* expert_offsets; /* device [num_experts + 1] */
+  const uint16_t* pair_weight;   /* device [num_pairs], bf16 bits */
+  const int32_t* token_pairs;    /* device [num_tokens][top_k] */
+  int64_t num_tokens;
+  int64_t num_pairs;
+  int32_t top_k;
+  int32_t num_experts;
+} qq_moe_plan;
+
+/* out[t] = sum over token t's pairs p (ascending expert) of
+ * down_e(silu(gate_e(x[t])) * up_e(x[t])) * pair_weight[p], with the bf16
+ * roundings of the reference's tensors (each projection's output, silu, the
+ * product, the weighted output, and every add into out).  x, out: bf16
+ * [tokens][hidden] rows x_stride / out_stride elements apart; w_gate / w_up
+ * (each [inter][hidden]) and w_down ([hidden][inter]) are device arrays of
+ * num_experts device pointers to row-major bf16 weights; h_buf (>= num_pairs x
+ * inter bf16) and y_buf (>= num_pairs x hidden bf16) are caller-owned
+ * scratch.  Three launches, no host synchronisation: the grouped GEMMs find
+ * each tile's expert on the device.  hidden a multiple of 256, inter of 128,
+ * top_k <= 16, num_experts <= 1024, 16-byte aligned rows; anything else
+ * returns QQ_ERR_UNSUPPORTED.  A pair token or pair index out of range is
+ * read as 0 / skipped and reported as QQ_DEV_ERR_BOUNDS in err (nullable).
+ * Replaces the expert loop of Qwen3MoeSparseMoeBlock.forward
+ * (model/qwen3_moe.py:139-147); the routing (qwen3_moe.py:133-138) is the
+ * caller's. */
+int qq_moe_experts(const qq_moe_plan* plan, const void* x, int64_t x_stride, int hidden, int inter,
+                   const void* const* w_gate, const void* const* w_up, const void* const* w_down, void* h_buf,
+                   void* y_buf, void* out, int64_t out_stride, uint32_t* err, void* stream);
+
 /* ---- [Q3] per-step bounds fold + finalize ----------------------------- */
 #define QQ_STEP_FOLD 1     /* running min/max <- key of the previous token */
 #define QQ_STEP_FINALIZE 2 /* finalize pages whose 64th token arrived, advance counters */

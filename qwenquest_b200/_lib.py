@@ -101,6 +101,19 @@ class QQHotBuffer(ctypes.Structure):
     ]
 
 
+class QQMoePlan(ctypes.Structure):
+    _fields_ = [
+        ("pair_token", c_void_p),
+        ("expert_offsets", c_void_p),
+        ("pair_weight", c_void_p),
+        ("token_pairs", c_void_p),
+        ("num_tokens", c_int64),
+        ("num_pairs", c_int64),
+        ("top_k", c_int32),
+        ("num_experts", c_int32),
+    ]
+
+
 class QQHostRing(ctypes.Structure):
     _fields_ = [("rows", c_void_p), ("state", c_void_p), ("capacity", c_int64)]
 
@@ -145,6 +158,9 @@ SIGNATURES: dict[str, tuple] = {
     "qq_extend_attention": (
         c_int, [_E, _T, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p, c_void_p,
                 c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
+    "qq_moe_experts": (
+        c_int, [POINTER(QQMoePlan), c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     "qq_quest_decode_step": (
         c_int, [_S, c_int, c_int, c_int, _PP, c_int, c_int64, _B, c_void_p, c_void_p, _T, c_int64,
                 c_void_p, c_size_t, c_void_p]),
@@ -244,6 +260,7 @@ __all__ = [
     "QQError",
     "QQExtendBatch",
     "QQHiSparseState",
+    "QQMoePlan",
     "QQHotBuffer",
     "QQNewToken",
     "QQQuestState",
