@@ -8,7 +8,9 @@ Drop-in attention backends for the reference's ``Engine``:
 plus :class:`~qwenquest_b200.quest.QuestAlgorithm` and
 :class:`~qwenquest_b200.hisparse.HiSparseCoordinator` with the reference's
 APIs, and :class:`~qwenquest_b200.graphs.DecodeStepGraph` (a decode step
-captured in a CUDA graph).  All decode work runs in hand-written CUDA kernels in ``libqquest.so``
+captured in a CUDA graph); :class:`~qwenquest_b200.moe.B200SparseMoeBlock` and
+:func:`~qwenquest_b200.moe.install_moe` (the model's MoE blocks on the tensor
+cores).  All decode work runs in hand-written CUDA kernels in ``libqquest.so``
 (C ABI: ``include/qquest.h``); nothing falls back to the CPU.  Importing this
 package does not load the library; the first backend / algorithm object does.
 """
@@ -18,10 +20,12 @@ __version__ = "0.1.0"
 __all__ = [
     "B200QuestHiSparseBackend",
     "B200QuestOnlyBackend",
+    "B200SparseMoeBlock",
     "DecodeStepGraph",
     "HiSparseCoordinator",
     "QuestAlgorithm",
     "QuestTrace",
+    "install_moe",
 ]
 
 
@@ -30,6 +34,10 @@ def __getattr__(name):
         from qwenquest_b200 import backends
 
         return getattr(backends, name)
+    if name in ("B200SparseMoeBlock", "install_moe"):
+        from qwenquest_b200 import moe
+
+        return getattr(moe, name)
     if name == "DecodeStepGraph":
         from qwenquest_b200.graphs import DecodeStepGraph
 
