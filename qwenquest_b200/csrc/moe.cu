@@ -21,7 +21,8 @@
 // so no host round trip is needed, and slots past the last tile exit.
 // Warp roles: warps 0-3 epilogue (thread = pair row = TMEM lane), warps 4-7
 // loaders (16-byte cp.async; pair rows gathered through their token index,
-// rows past the expert's pairs zero-filled without a read), warp 8 TMEM
+// rows past the expert's pairs zero-filled without a read; each thread's
+// copies of a stage arrive on its barrier asynchronously), warp 8 TMEM
 // allocation and MMA issue (one thread).  Every mbarrier wait is bounded.
 
 #include <cmath>
@@ -46,7 +47,6 @@ constexpr int kThreads = (kMmaWarp + 1) * 32;     // 288
 constexpr int kDynSmem = kStages * kStageBytes + 1024;
 constexpr uint32_t kTmemCols = 256;
 constexpr int kMaxExperts = 1024;
-constexpr int kLag = 2;  // stages in flight per loader thread beyond the newest
 
 enum : int { kBarFull = 0, kBarEmpty = kStages, kBarDone = 2 * kStages, kNumBars = kBarDone + 1 };
 
@@ -167,21 +167,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(MoeArgs a) {
     }
     const char* w0 = static_cast<const char*>(a.w0[e]);
     const char* w1 = MODE == 0 ? static_cast<const char*>(a.w1[e]) : nullptr;
-    bool ok = true;
-    int sig = 0;
 #pragma unroll 1
     for (int t = 0; t < KB; ++t) {
       const int st = t % kStages;
-      if (t >= kStages) {
-        const uint32_t par = ((t / kStages) - 1) & 1;
-        if (!__all_sync(0xffffffffu, mbar_try_wait(bar(kBarEmpty + st), par))) {
-          cp_async_wait<0>();
-          fence_async_shared();
-          for (; sig < t; ++sig) mbar_arrive(bar(kBarFull + sig % kStages));
-          ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarEmpty + st), par, abort_flag, a.err));
-          if (!ok) break;
-        }
-      }
+      if (t >= kStages &&
+          !__all_sync(0xffffffffu, mbar_wait(bar(kBarEmpty + st), ((t / kStages) - 1) & 1, abort_flag, a.err)))
+        break;
       const uint32_t sa = base + st * kStageBytes, sb = sa + kABytes;
       const int64_t koff = (int64_t)t * (kMK * 2);
 #pragma unroll
@@ -199,18 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(MoeArgs a) {
         else src = w0 + (int64_t)(c0 + r) * a.w_stride;
         cp_async_16(sb + r * 128 + (((ch ^ (r & 7))) << 4), src + koff + ch * 16);
       }
-      cp_async_commit();
-      if (t - sig == kLag) {
-        cp_async_wait<kLag>();
-        fence_async_shared();
-        mbar_arrive(bar(kBarFull + sig % kStages));
-        ++sig;
-      }
+      cp_async_arrive(bar(kBarFull + st));
     }
     cp_async_wait<0>();
-    fence_async_shared();
-    if (ok)
-      for (; sig < KB; ++sig) mbar_arrive(bar(kBarFull + sig % kStages));
   } else if (warp == kMmaWarp) {
     // ================================================================ MMA issue
     if (lane == 0) {
@@ -223,9 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(MoeArgs a) {
         if (!ok) break;
         tc_fence_after();
         const uint64_t da = desc_k(base + st * kStageBytes), db = desc_k(base + st * kStageBytes + kABytes);
-#pragma unroll
-        for (int kk = 0; kk < kMK / 16; ++kk)
-          umma_bf16(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), kId, (t > 0 || kk > 0) ? 1u : 0u);
+        umma_bf16_x4(tmem, da, db, 2, 2, kId, t > 0 ? 1u : 0u);  // four 32-byte k-steps
         umma_commit(bar(kBarEmpty + st));
       }
       umma_commit(bar(kBarDone));

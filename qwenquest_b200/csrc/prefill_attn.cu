@@ -18,7 +18,9 @@
 //   warps 4-7  softmax of head 1
 //   warps 8-11 loaders: Q tiles once, then K_0 V_0 K_1 V_1 ... through a ring
 //              of ten 16 KiB slots, 16-byte cp.async row gathers into the
-//              128-byte-swizzled layouts the MMA descriptors name
+//              128-byte-swizzled layouts the MMA descriptors name; each
+//              thread's copies of a tile arrive on its barrier asynchronously
+//              (cp.async.mbarrier.arrive), so the loaders never wait for data
 //   warp 12    TMEM allocation; lane 0 issues every tcgen05.mma
 // Tensor memory (512 columns): per head h two score buffers S_h[0], S_h[1]
 // (fp32 128 x 64) and the output O_h (fp32 128 x 128).
@@ -186,42 +188,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(PrefillArgs a
         cp_async_16_zfill(qdst + hh * kQBytes + sw128(r, chunk, kQHalf), src, ok ? 16u : 0u);
       }
     }
-    cp_async_commit();
-    cp_async_wait<0>();
-    fence_async_shared();
-    mbar_arrive(bar(kBarQ));
+    cp_async_arrive(bar(kBarQ));
 
     // each warp moves 16 key rows of a tile: rows lw * 16 + 2 i + half, i < 8.
     // Keys past kv_end carry kPastEnd and are zero-filled.
     // Lanes 0-15 (and 16-31, the same) hold the pool rows of the warp's 16
     // keys of the current key tile; the next tile's are loaded one tile ahead.
-    // Up to kLag + 1 tiles are in flight per thread; a tile is announced
-    // (full barrier) once its copies are done, and before blocking on a busy
-    // slot the warp announces every tile it issued, since the consumer may
-    // need them to free that slot.
-    constexpr int kLag = 4;
+    // Each thread's copies of a tile count on the tile's full barrier by an
+    // asynchronous arrival (cp.async.mbarrier.arrive), so tiles are in flight
+    // as deep as the ring allows, with no wait on the loaders' side.
     auto key_row = [&](int j) -> int32_t {
       const int64_t kp = (int64_t)j * kPN + lw * 16 + (lane & 15);
       return kp < kv_end ? __ldg(a.r2t + req * a.r2t_stride + kp) : kPastEnd;
     };
     int32_t row_next = key_row(0);
     int32_t myrow = kPastEnd;
-    bool ok = true;
-    int sig = 0;  // tiles [sig, t) are issued but not announced
     const int T = 2 * nkv;
 #pragma unroll 1
     for (int t = 0; t < T; ++t) {
       const int slot = t % kRing;
-      if (t >= kRing) {
-        const uint32_t par = ((t / kRing) - 1) & 1;
-        if (!__all_sync(0xffffffffu, mbar_try_wait(bar(kBarEmpty + slot), par))) {
-          cp_async_wait<0>();
-          fence_async_shared();
-          for (; sig < t; ++sig) mbar_arrive(bar(kBarFull + sig % kRing));
-          ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarEmpty + slot), par, abort_flag, a.err));
-          if (!ok) break;
-        }
-      }
+      if (t >= kRing &&
+          !__all_sync(0xffffffffu, mbar_wait(bar(kBarEmpty + slot), ((t / kRing) - 1) & 1, abort_flag, a.err)))
+        break;
       const bool is_v = (t & 1) != 0;
       if (!is_v) {
         const int j = t >> 1;
@@ -241,18 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(PrefillArgs a
         cp_async_16_zfill(dst + sw128(r, chunk, kKVHalf), pool + (int64_t)(row < 0 ? 0 : row) * a.row_bytes,
                           row >= 0 ? 16u : 0u);
       }
-      cp_async_commit();
-      if (t - sig == kLag) {
-        cp_async_wait<kLag>();
-        fence_async_shared();
-        mbar_arrive(bar(kBarFull + sig % kRing));
-        ++sig;
-      }
+      cp_async_arrive(bar(kBarFull + slot));
     }
     cp_async_wait<0>();
-    fence_async_shared();
-    if (ok)
-      for (; sig < T; ++sig) mbar_arrive(bar(kBarFull + sig % kRing));
   } else if (warp == kMmaWarp) {
     // ================================================================ MMA issue
     if (lane == 0) {
@@ -265,23 +244,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(PrefillArgs a
       const uint64_t dQ0 = desc_k(base + kOffQ), dQ1 = desc_k(base + kOffQ + kQBytes);
       auto slot_addr = [&](int t) { return base + kOffKV + (uint32_t)(t % kRing) * kKVBytes; };
       // S_h(j) = Q_h . K_j^T into buffer b: M 128, N 64, K 128 in eight steps
+      // (two 64-column blocks of four 32-byte steps each)
       auto qk = [&](int h, int b, uint32_t ks) {
         const uint64_t dq = h ? dQ1 : dQ0;
         const uint64_t dk = desc_k(ks);
         const uint32_t d = tS(h, b);
-#pragma unroll
-        for (int kk = 0; kk < kPD / 16; ++kk)
-          umma_bf16(d, dq + (uint64_t)(((kk >> 2) * kQHalf + (kk & 3) * 32) >> 4),
-                    dk + (uint64_t)(((kk >> 2) * kKVHalf + (kk & 3) * 32) >> 4), kIdQK, kk > 0);
+        umma_bf16_x4(d, dq, dk, 2, 2, kIdQK, 0u);
+        umma_bf16_x4(d, dq + (uint64_t)(kQHalf >> 4), dk + (uint64_t)(kKVHalf >> 4), 2, 2, kIdQK, 1u);
       };
       // O_h += P_h(b) . V_j: M 128, N 128, K 64 in four steps, P from tensor
       // memory (8 columns of bf16 pairs per step)
       auto pv = [&](int h, int b, uint32_t vs, bool acc) {
-        const uint64_t dv = desc_mn(vs, kKVHalf);
-        const uint32_t d = tO(h), pa = tS(h, b);
-#pragma unroll
-        for (int kk = 0; kk < kPN / 16; ++kk)
-          umma_bf16_ts(d, pa + kk * 8, dv + (uint64_t)((kk * 16 * 128) >> 4), kIdPV, (acc || kk > 0) ? 1u : 0u);
+        umma_bf16_ts_x4(tO(h), tS(h, b), desc_mn(vs, kKVHalf), 8, (16 * 128) >> 4, kIdPV, acc ? 1u : 0u);
       };
       auto wait_full = [&](int t) {
         return mbar_wait(bar(kBarFull + t % kRing), (t / kRing) & 1, abort_flag, a.err);

@@ -56,6 +56,38 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
+// Four MMAs into one accumulator, issued back to back from one asm block: A
+// and B descriptors advance by a_step / b_step (in 16-byte units) per MMA;
+// the first MMA accumulates when acc != 0, the others always.
+__device__ __forceinline__ void umma_bf16_x4(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t a_step,
+                                             uint32_t b_step, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p, t;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\tsetp.eq.b32 t, %5, %5;\n\t"
+      "add.s64 a1, %1, %6;\n\tadd.s64 a2, a1, %6;\n\tadd.s64 a3, a2, %6;\n\t"
+      "add.s64 b1, %2, %7;\n\tadd.s64 b2, b1, %7;\n\tadd.s64 b3, b2, %7;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, t;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, t;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, t;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "n"(0), "r"(acc), "l"((uint64_t)a_step), "l"((uint64_t)b_step)
+      : "memory");
+}
+// The same with A read from tensor memory: its column advances by a_step per MMA.
+__device__ __forceinline__ void umma_bf16_ts_x4(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t a_step,
+                                                uint32_t b_step, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p, t;\n\t.reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\tsetp.eq.b32 t, %5, %5;\n\t"
+      "add.u32 a1, %1, %6;\n\tadd.u32 a2, a1, %6;\n\tadd.u32 a3, a2, %6;\n\t"
+      "add.s64 b1, %2, %7;\n\tadd.s64 b2, b1, %7;\n\tadd.s64 b3, b2, %7;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, t;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, t;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, t;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "n"(0), "r"(acc), "r"(a_step), "l"((uint64_t)b_step)
+      : "memory");
+}
 // The mbarrier gets one arrival once every tcgen05 operation this thread issued before has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -70,6 +102,12 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}\n" ::"r"(bar) : "memory");
+}
+// One arrival on the mbarrier, made by the hardware once every cp.async this
+// thread issued before has completed (counts against the barrier's expected
+// arrivals).  The tensor core may read the copied data once the phase completes.
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
