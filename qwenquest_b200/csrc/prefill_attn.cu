@@ -13,7 +13,7 @@
 // query heads of the same KV head group (32 / 4 heads: 16 pairs), so every
 // K/V tile brought into shared memory serves two products.  Keys go in
 // tiles of 64.
-// Warp roles, 13 warps:
+// Warp roles, 14 warps:
 //   warps 0-3  softmax of head 0 of the pair (thread = query row = TMEM lane)
 //   warps 4-7  softmax of head 1
 //   warps 8-11 loaders: Q tiles once, then K_0 V_0 K_1 V_1 ... through a ring
@@ -21,11 +21,13 @@
 //              128-byte-swizzled layouts the MMA descriptors name; each
 //              thread's copies of a tile arrive on its barrier asynchronously
 //              (cp.async.mbarrier.arrive), so the loaders never wait for data
-//   warp 12    TMEM allocation; lane 0 issues every tcgen05.mma
+//   warps 12-13 one per head: lane 0 issues that head's tcgen05.mma (one
+//              issuing thread for both heads measured 0.76x as fast: the
+//              issue of the small MMAs, not the tensor pipe, set the pace);
+//              warp 12 also allocates the tensor memory
 // Tensor memory (512 columns): per head h two score buffers S_h[0], S_h[1]
 // (fp32 128 x 64) and the output O_h (fp32 128 x 128).
-// MMA issue order per key tile j (b = j mod 2):
-//   PV_0(j) S_0(j+2) PV_1(j) S_1(j+2)
+// MMA issue order of head h per key tile j (b = j mod 2): PV_h(j) S_h(j+2),
 // with S_h(j+2) into the buffer the softmax of tile j just released, so the
 // scores of the next tile are ready while a head's softmax of tile j runs.
 // P_h(j) (bf16 pairs) replaces the first 32 columns of its score buffer and
@@ -61,8 +63,8 @@ constexpr int kKVHalf = kKVBytes / 2;        // one 64-column block of K or V
 constexpr int kRing = 10;                    // K / V slots
 constexpr int kSoftWarps = 8;
 constexpr int kLoadWarps = 4;
-constexpr int kMmaWarp = kSoftWarps + kLoadWarps;  // 12
-constexpr int kThreads = (kMmaWarp + 1) * 32;      // 416
+constexpr int kMmaWarp = kSoftWarps + kLoadWarps;  // 12: the first of two MMA warps
+constexpr int kThreads = (kMmaWarp + 2) * 32;      // 448: one MMA warp per head
 constexpr int kOffQ = 0;
 constexpr int kOffKV = 2 * kQBytes;
 constexpr int kDynSmem = kOffKV + kRing * kKVBytes + 1024;  // + slack to align the base to 1024
@@ -70,10 +72,11 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kRaise = 8.0f;  // log2 of the largest unscaled weight
 constexpr int32_t kPastEnd = INT32_MIN;  // pool row of a key past the request's keys
 
-// mbarrier slots: Q; ring full / empty; per head and buffer S full, P full;
-// per head one arrival per finished P.V; the final commit
+// mbarrier slots: Q; ring full / empty (a slot is free once both heads'
+// MMAs that read it are done: two commits); per head and buffer S full,
+// P full; per head one arrival per finished P.V; per head the final commit
 enum : int { kBarQ = 0, kBarFull = 1, kBarEmpty = kBarFull + kRing, kBarS = kBarEmpty + kRing,
-             kBarP = kBarS + 4, kBarODone = kBarP + 4, kBarO = kBarODone + 2, kNumBars = kBarO + 1 };
+             kBarP = kBarS + 4, kBarODone = kBarP + 4, kBarO = kBarODone + 2, kNumBars = kBarO + 2 };
 
 struct PrefillArgs {
   const int64_t* req_idx;
@@ -154,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(PrefillArgs a
     mbar_init(bar(kBarQ), kLoadWarps * 32);
     for (int i = 0; i < kRing; ++i) {
       mbar_init(bar(kBarFull + i), kLoadWarps * 32);
-      mbar_init(bar(kBarEmpty + i), 1);
+      mbar_init(bar(kBarEmpty + i), 2);
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(bar(kBarS + i), 1);
@@ -163,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(PrefillArgs a
     mbar_init(bar(kBarODone + 0), 1);
     mbar_init(bar(kBarODone + 1), 1);
     mbar_init(bar(kBarO), 1);
+    mbar_init(bar(kBarO + 1), 1);
     mbar_init_fence();
   }
   if (warp == kMmaWarp) {
@@ -232,78 +236,59 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(PrefillArgs a
       cp_async_arrive(bar(kBarFull + slot));
     }
     cp_async_wait<0>();
-  } else if (warp == kMmaWarp) {
+  } else if (warp >= kMmaWarp) {
     // ================================================================ MMA issue
     if (lane == 0) {
+      const int h = warp - kMmaWarp;  // this warp issues head h's MMAs
       constexpr uint32_t kIdQK = instr_desc(0, kPM, kPN);
       constexpr uint32_t kIdPV = instr_desc(1, kPM, kPD);
-      auto tS = [&](int h, int b) { return tmem + h * 256 + b * 64; };
-      auto tO = [&](int h) { return tmem + h * 256 + 128; };
-      // descriptors are built once per operand; a k-step adds its byte
-      // offset >> 4 to the start-address field (no carry: addresses < 256 KiB)
-      const uint64_t dQ0 = desc_k(base + kOffQ), dQ1 = desc_k(base + kOffQ + kQBytes);
+      auto tS = [&](int b) { return tmem + h * 256 + b * 64; };
+      const uint32_t tO = tmem + h * 256 + 128;
+      const uint64_t dq = desc_k(base + kOffQ + h * kQBytes);
       auto slot_addr = [&](int t) { return base + kOffKV + (uint32_t)(t % kRing) * kKVBytes; };
-      // S_h(j) = Q_h . K_j^T into buffer b: M 128, N 64, K 128 in eight steps
-      // (two 64-column blocks of four 32-byte steps each)
-      auto qk = [&](int h, int b, uint32_t ks) {
-        const uint64_t dq = h ? dQ1 : dQ0;
+      auto qk = [&](int b, uint32_t ks) {
         const uint64_t dk = desc_k(ks);
-        const uint32_t d = tS(h, b);
-        umma_bf16_x4(d, dq, dk, 2, 2, kIdQK, 0u);
-        umma_bf16_x4(d, dq + (uint64_t)(kQHalf >> 4), dk + (uint64_t)(kKVHalf >> 4), 2, 2, kIdQK, 1u);
+        umma_bf16_x4(tS(b), dq, dk, 2, 2, kIdQK, 0u);
+        umma_bf16_x4(tS(b), dq + (uint64_t)(kQHalf >> 4), dk + (uint64_t)(kKVHalf >> 4), 2, 2, kIdQK, 1u);
       };
-      // O_h += P_h(b) . V_j: M 128, N 128, K 64 in four steps, P from tensor
-      // memory (8 columns of bf16 pairs per step)
-      auto pv = [&](int h, int b, uint32_t vs, bool acc) {
-        umma_bf16_ts_x4(tO(h), tS(h, b), desc_mn(vs, kKVHalf), 8, (16 * 128) >> 4, kIdPV, acc ? 1u : 0u);
+      auto pv = [&](int b, uint32_t vs, bool acc) {
+        umma_bf16_ts_x4(tO, tS(b), desc_mn(vs, kKVHalf), 8, (16 * 128) >> 4, kIdPV, acc ? 1u : 0u);
       };
       auto wait_full = [&](int t) {
         return mbar_wait(bar(kBarFull + t % kRing), (t / kRing) & 1, abort_flag, a.err);
       };
       bool ok = mbar_wait(bar(kBarQ), 0, abort_flag, a.err);
-      // the scores of the first two key tiles
 #pragma unroll 1
       for (int jj = 0; jj < 2 && jj < nkv && ok; ++jj) {
         ok = wait_full(2 * jj);
         if (!ok) break;
         tc_fence_after();
-        qk(0, jj, slot_addr(2 * jj));
-        umma_commit(bar(kBarS + 0 * 2 + jj));
-        qk(1, jj, slot_addr(2 * jj));
-        umma_commit(bar(kBarS + 1 * 2 + jj));
+        qk(jj, slot_addr(2 * jj));
+        umma_commit(bar(kBarS + 2 * h + jj));
         umma_commit(bar(kBarEmpty + (2 * jj) % kRing));
       }
 #pragma unroll 1
       for (int j = 0; j < nkv && ok; ++j) {
         const int b = j & 1;
-        const int tv = 2 * j + 1, tk = 2 * j + 4;  // V_j, K_(j+2)
+        const int tv = 2 * j + 1, tk = 2 * j + 4;
         const bool more = j + 2 < nkv;
-        ok = wait_full(tv);
+        ok = wait_full(tv) && mbar_wait(bar(kBarP + 2 * h + b), (j >> 1) & 1, abort_flag, a.err);
         if (!ok) break;
-#pragma unroll 1
-        for (int h = 0; h < 2 && ok; ++h) {
-          ok = mbar_wait(bar(kBarP + 2 * h + b), (j >> 1) & 1, abort_flag, a.err);
+        tc_fence_after();
+        pv(b, slot_addr(tv), j > 0);
+        umma_commit(bar(kBarODone + h));
+        umma_commit(bar(kBarEmpty + tv % kRing));
+        if (more) {
+          ok = wait_full(tk);
           if (!ok) break;
           tc_fence_after();
-          pv(h, b, slot_addr(tv), j > 0);
-          umma_commit(bar(kBarODone + h));
-          if (more) {
-            if (h == 0) {
-              ok = wait_full(tk);
-              if (!ok) break;
-              tc_fence_after();
-            }
-            qk(h, b, slot_addr(tk));
-            umma_commit(bar(kBarS + 2 * h + b));
-          }
+          qk(b, slot_addr(tk));
+          umma_commit(bar(kBarS + 2 * h + b));
+          umma_commit(bar(kBarEmpty + tk % kRing));
         }
-        if (!ok) break;
-        umma_commit(bar(kBarEmpty + tv % kRing));
-        if (more) umma_commit(bar(kBarEmpty + tk % kRing));
       }
-      // every MMA issued above has completed when this arrives (also after giving up)
-      umma_commit(bar(kBarO));
-      mbar_wait(bar(kBarO), 0, abort_flag, a.err, true);
+      umma_commit(bar(kBarO + h));
+      mbar_wait(bar(kBarO + h), 0, abort_flag, a.err, true);
     }
     __syncwarp();
   } else {
@@ -390,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(PrefillArgs a
       mbar_arrive(bar(kBarP + 2 * hh + b));
     }
     // ---- epilogue: O / l in the query dtype
-    ok = __all_sync(0xffffffffu, ok && mbar_wait(bar(kBarO), 0, abort_flag, a.err));
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(bar(kBarO + hh), 0, abort_flag, a.err));
     tc_fence_after();
     const bool valid = ok && t0 + r < n;
     const float inv = l > 0.f ? 1.f / l : 0.f;
