@@ -86,6 +86,44 @@ def test_extend_argument_errors_are_reported_without_touching_a_device(lib):
     assert call(None, eb, hot=hot) == inv                            # hot buffer without V
 
 
+def test_prefill_attention_and_moe_argument_errors_without_a_device(lib):
+    """qq_extend_attention and qq_moe_experts check their arguments before any CUDA call."""
+    ok, inv, uns = _lib.QQ_OK, _lib.QQ_ERR_INVALID, _lib.QQ_ERR_UNSUPPORTED
+    eb = _lib.QQExtendBatch(0x1000, 0x2000, 0x3000, 0x4000, 0, 8, 1, 8)
+    table = _lib.QQTokenTable(0x10000, 64, 4)
+
+    def attn(batch=eb, tbl=table, tiles=0x5000, n_tiles=1, q=0x20000, dtype=_lib.QQ_BF16, heads=32, kv=4, d=128,
+             q_stride=4096, k=0x30000, v=0x40000, row=512, rows=100, out=0x50000, out_stride=4096):
+        return lib.qq_extend_attention(batch, tbl, tiles, n_tiles, q, dtype, heads, kv, d, q_stride, k, v, row, rows,
+                                       0.088, out, out_stride, None, None)
+
+    assert attn(batch=None) == inv
+    assert attn(tbl=_lib.QQTokenTable()) == inv                   # no req_to_token
+    assert attn(q=0) == inv
+    assert attn(heads=30, kv=4) == inv                             # heads not a multiple of KV heads
+    assert attn(n_tiles=0) == ok                                   # nothing to do
+    assert attn(tiles=0) == inv
+    assert attn(dtype=_lib.QQ_F32) == uns                          # the tcgen05 kernel is bf16 only
+    assert attn(d=64) == uns                                       # head_dim 128 only
+    assert attn(heads=12, kv=4) == uns                             # 3 query heads per KV head: not in pairs
+    assert attn(q=0x20008) == uns                                  # rows must be 16-byte aligned
+    assert attn(n_tiles=70000) == uns
+
+    plan = _lib.QQMoePlan(0x1000, 0x2000, 0x3000, 0x4000, 8, 64, 8, 128)
+
+    def moe(p=plan, x=0x10000, hidden=2048, inter=768, wg=0x20000, out=0x30000):
+        return lib.qq_moe_experts(p, x, hidden, hidden, inter, wg, 0x21000, 0x22000, 0x40000, 0x50000, out, hidden,
+                                  None, None)
+
+    assert moe(p=None) == inv
+    assert moe(wg=0) == inv
+    assert moe(p=_lib.QQMoePlan(0x1000, 0x2000, 0x3000, 0x4000, 0, 0, 8, 128)) == ok   # no tokens
+    assert moe(hidden=2000) == uns                                  # hidden a multiple of 256
+    assert moe(inter=700) == uns                                    # intermediate a multiple of 128
+    assert moe(p=_lib.QQMoePlan(0x1000, 0x2000, 0x3000, 0x4000, 8, 64, 17, 128)) == uns  # top_k <= 16
+    assert moe(x=0x10008) == uns
+
+
 def test_device_error_bits_map_to_reference_exceptions():
     with pytest.raises(RuntimeError):
         _lib.raise_device_error(_lib.QQ_DEV_ERR_CAPACITY)
