@@ -1,7 +1,8 @@
 """Drop-in for the reference's ``Qwen3MoeSparseMoeBlock`` (``model/qwen3_moe.py:121-147``).
 
-:class:`B200SparseMoeBlock` wraps a reference block and shares its parameters
-(nothing is copied).  ``forward`` computes the routing with the reference's
+:class:`B200SparseMoeBlock` is a subclass of the reference block that takes
+over a block's own ``gate`` and ``experts`` modules (nothing is copied, and
+the parameter names of the model's ``state_dict`` stay the same).  ``forward`` computes the routing with the reference's
 own torch operations (``qwen3_moe.py:133-138``: gate logits, fp32 softmax,
 top-k, renormalisation, cast to the logits' dtype), groups the (token, slot)
 pairs by expert with a stable sort (tokens ascending within an expert, the
@@ -46,14 +47,21 @@ def moe_plan(experts: torch.Tensor, weights: torch.Tensor, num_experts: int):
     return pair_token, pair_weight, offsets, token_pairs.view(tokens, k)
 
 
-class B200SparseMoeBlock(nn.Module):
+def _reference_block_class():
+    from qwenquest.model.qwen3_moe import Qwen3MoeSparseMoeBlock
+
+    return Qwen3MoeSparseMoeBlock
+
+
+class B200SparseMoeBlock(_reference_block_class()):
     """The reference block's computation with its expert loop on the B200 kernels."""
 
     def __init__(self, block: nn.Module):
-        super().__init__()
-        self.block = block  # the reference module: parameters, routing constants, fallback forward
+        nn.Module.__init__(self)  # the block's modules are adopted, not rebuilt
         self.top_k = block.top_k
         self.norm_topk_prob = block.norm_topk_prob
+        self.gate = block.gate
+        self.experts = block.experts
         self._tables = None
         self._key = None
         self._err = torch.zeros(1, dtype=torch.int32).pin_memory() if torch.cuda.is_available() else None
@@ -62,13 +70,13 @@ class B200SparseMoeBlock(nn.Module):
     # ------------------------------------------------------------ weights
 
     def _weights(self):
-        ex = self.block.experts
+        ex = self.experts
         return ([m.gate_proj.weight for m in ex], [m.up_proj.weight for m in ex], [m.down_proj.weight for m in ex])
 
     def _state(self, device):
         """Per-device pointer tables and the geometry check, built once (rebuilt if the
         weights moved: their first and last pointers are compared on every call)."""
-        ex = self.block.experts
+        ex = self.experts
         key = (device, ex[0].gate_proj.weight.data_ptr(), ex[-1].down_proj.weight.data_ptr())
         if self._key != key:
             gate, up, down = self._weights()
@@ -95,10 +103,9 @@ class B200SparseMoeBlock(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not self.supported(x):
-            return self.block(x)
-        blk = self.block
+            return super().forward(x)
         # routing: the reference's own operations (qwen3_moe.py:133-138)
-        router_logits = blk.gate(x)
+        router_logits = self.gate(x)
         probs = F.softmax(router_logits, dim=-1, dtype=torch.float32)
         weights, experts = torch.topk(probs, self.top_k, dim=-1)
         if self.norm_topk_prob:
@@ -145,7 +152,7 @@ def install_moe(model: nn.Module) -> int:
 
     n = 0
     for layer in model.model.layers:
-        if isinstance(layer.mlp, Qwen3MoeSparseMoeBlock):
+        if isinstance(layer.mlp, Qwen3MoeSparseMoeBlock) and not isinstance(layer.mlp, B200SparseMoeBlock):
             layer.mlp = B200SparseMoeBlock(layer.mlp)
             n += 1
     return n
