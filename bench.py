@@ -1466,6 +1466,9 @@ def main() -> None:
             "layer_step_bytes": step_bytes,
             "layer_step_gbs": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 1e9,
             "layer_step_frac_of_peak": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 1e9 / peak,
+            # the same against the nominal 8 TB/s of B200 HBM3e, and per request
+            "layer_step_frac_of_nominal_8tbs": step_bytes / (ms / 1e3 / (n_layers * args.steps)) / 8e12,
+            "request_layer_steps_per_s_per_gpu": n_req * (n_layers * args.steps) / (ms / 1e3),
             "kernel_ms": kernel_ms,
             "path": value_path,
             "paths": {
