@@ -240,6 +240,18 @@ typedef struct qq_moe_plan {
   int32_t num_experts;
 } qq_moe_plan;
 
+/* The plan of a small routing in one launch: experts and weights (bf16 bits)
+ * are device [num_tokens][top_k] (torch.topk's indices and the cast
+ * weights); writes pair_token, pair_weight, expert_offsets ([num_experts + 1])
+ * and token_pairs as the qq_moe_plan struct describes them, pairs ascending by expert
+ * and by token within an expert.  num_tokens * top_k <= 2048 and
+ * num_experts <= 1024, else QQ_ERR_UNSUPPORTED (larger batches sort with a
+ * library routine).  Replaces the grouping the reference's loop makes with
+ * torch.unique / torch.where (model/qwen3_moe.py:141-142). */
+int qq_moe_route_plan(const int64_t* experts, const uint16_t* weights, int64_t num_tokens, int top_k, int num_experts,
+                      int32_t* pair_token, uint16_t* pair_weight, int64_t* expert_offsets, int32_t* token_pairs,
+                      uint32_t* err, void* stream);
+
 /* out[t] = sum over token t's pairs p (ascending expert) of
  * down_e(silu(gate_e(x[t])) * up_e(x[t])) * pair_weight[p], with the bf16
  * roundings of the reference's tensors (each projection's output, silu, the

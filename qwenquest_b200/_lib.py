@@ -158,6 +158,9 @@ SIGNATURES: dict[str, tuple] = {
     "qq_extend_attention": (
         c_int, [_E, _T, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_void_p, c_void_p,
                 c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
+    "qq_moe_route_plan": (
+        c_int, [c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                c_void_p]),
     "qq_moe_experts": (
         c_int, [POINTER(QQMoePlan), c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                 c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),

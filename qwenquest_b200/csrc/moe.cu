@@ -316,6 +316,62 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* token_p
   }
 }
 
+// The routing's pairs grouped by expert in one CTA (small batches): thread e
+// counts expert e's pairs, a block scan gives the offsets, then thread e
+// walks the pairs in (token, slot) order and places its own, so the order
+// within an expert is ascending token (the reference loop's torch.where
+// order) with no atomics.  An expert index out of range is skipped and
+// reported.
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanMaxPairs = 2048;
+
+__global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const int64_t* experts, const uint16_t* weights,
+                                                                int num_pairs, int top_k, int num_experts,
+                                                                int32_t* pair_token, uint16_t* pair_weight,
+                                                                int64_t* offsets, int32_t* token_pairs, uint32_t* err) {
+  __shared__ int16_t s_ex[kPlanMaxPairs];
+  __shared__ int32_t s_off[kMaxExperts + 1];
+  for (int i = threadIdx.x; i < num_pairs; i += blockDim.x) {
+    const int64_t e = experts[i];
+    if (e < 0 || e >= num_experts) {
+      raise_error(err, QQ_DEV_ERR_BOUNDS);
+      s_ex[i] = -1;
+      token_pairs[i] = 0;
+    } else {
+      s_ex[i] = (int16_t)e;
+    }
+  }
+  __syncthreads();
+  const int e = threadIdx.x;
+  int cnt = 0;
+  if (e < num_experts)
+    for (int i = 0; i < num_pairs; ++i) cnt += s_ex[i] == e;
+  // exclusive scan of the counts over the block (experts <= blockDim)
+  s_off[threadIdx.x + 1] = cnt;
+  if (threadIdx.x == 0) s_off[0] = 0;
+  __syncthreads();
+  for (int o = 1; o < kPlanThreads; o <<= 1) {
+    const int t = threadIdx.x + 1;
+    const int val = t > o ? s_off[t - o] : 0;
+    __syncthreads();
+    s_off[t] += val;
+    __syncthreads();
+  }
+  if (e < num_experts) {
+    const int base = s_off[e];
+    offsets[e] = base;
+    if (e == num_experts - 1) offsets[num_experts] = s_off[num_experts];
+    int run = 0;
+    for (int i = 0; i < num_pairs; ++i) {
+      if (s_ex[i] != e) continue;
+      const int p = base + run++;
+      pair_token[p] = i / top_k;
+      pair_weight[p] = weights[i];
+      token_pairs[i] = p;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace qq
 
@@ -382,5 +438,19 @@ extern "C" int qq_moe_experts(const qq_moe_plan* plan, const void* x, int64_t x_
   moe_combine_kernel<<<(unsigned)plan->num_tokens, 256, 0, s>>>(
       plan->token_pairs, plan->top_k, static_cast<const char*>(y_buf), (int64_t)hidden * 2, hidden, plan->num_pairs,
       static_cast<char*>(out), out_stride * 2, err);
+  return launch_status();
+}
+
+extern "C" int qq_moe_route_plan(const int64_t* experts, const uint16_t* weights, int64_t num_tokens, int top_k,
+                           int num_experts, int32_t* pair_token, uint16_t* pair_weight, int64_t* expert_offsets,
+                           int32_t* token_pairs, uint32_t* err, void* stream) {
+  using namespace qq;
+  if (experts == nullptr || weights == nullptr || pair_token == nullptr || pair_weight == nullptr ||
+      expert_offsets == nullptr || token_pairs == nullptr || num_tokens < 0 || top_k <= 0 || num_experts <= 0)
+    return QQ_ERR_INVALID;
+  if (num_experts > kMaxExperts || num_tokens * top_k > kPlanMaxPairs) return QQ_ERR_UNSUPPORTED;
+  moe_plan_kernel<<<1, kPlanThreads, 0, as_stream(stream)>>>(experts, weights, (int)(num_tokens * top_k), top_k,
+                                                             num_experts, pair_token, pair_weight, expert_offsets,
+                                                             token_pairs, err);
   return launch_status();
 }

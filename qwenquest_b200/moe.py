@@ -5,8 +5,9 @@ over a block's own ``gate`` and ``experts`` modules (nothing is copied, and
 the parameter names of the model's ``state_dict`` stay the same).  ``forward`` computes the routing with the reference's
 own torch operations (``qwen3_moe.py:133-138``: gate logits, fp32 softmax,
 top-k, renormalisation, cast to the logits' dtype), groups the (token, slot)
-pairs by expert with a stable sort (tokens ascending within an expert, the
-order ``torch.where`` gives the reference's loop), and runs the expert loop
+pairs by expert, tokens ascending within an expert (the order ``torch.where``
+gives the reference's loop: one ``qq_moe_route_plan`` launch for small
+batches, a stable torch sort for large ones), and runs the expert loop
 (``qwen3_moe.py:139-147``) as one ``qq_moe_experts`` call: two grouped GEMMs
 on the tcgen05 tensor cores and a combine, no host synchronisation.
 Geometries the kernels do not take (not bf16, hidden not a multiple of 256,
@@ -27,7 +28,7 @@ from qwenquest_b200 import _lib
 from qwenquest_b200._lib import check
 from qwenquest_b200.quest import stream_of
 
-__all__ = ["B200SparseMoeBlock", "install_moe", "moe_plan"]
+__all__ = ["B200SparseMoeBlock", "device_moe_plan", "install_moe", "moe_plan"]
 
 
 def moe_plan(experts: torch.Tensor, weights: torch.Tensor, num_experts: int):
@@ -51,6 +52,29 @@ def _reference_block_class():
     from qwenquest.model.qwen3_moe import Qwen3MoeSparseMoeBlock
 
     return Qwen3MoeSparseMoeBlock
+
+
+#: routings of at most this many (token, slot) pairs are grouped by one qq_moe_route_plan launch
+ROUTE_PLAN_MAX_PAIRS = 2048
+
+
+def device_moe_plan(experts: torch.Tensor, weights: torch.Tensor, num_experts: int, err_ptr=None):
+    """:func:`moe_plan` in one ``qq_moe_route_plan`` launch (CUDA tensors, at most
+    ``ROUTE_PLAN_MAX_PAIRS`` pairs); the same arrays, bit for bit."""
+    tokens, k = experts.shape
+    dev = experts.device
+    experts = experts.to(torch.int64).contiguous()
+    weights = weights.to(torch.bfloat16).contiguous()
+    pairs = tokens * k
+    pair_token = torch.empty(pairs, dtype=torch.int32, device=dev)
+    pair_weight = torch.empty(pairs, dtype=torch.bfloat16, device=dev)
+    offsets = torch.empty(num_experts + 1, dtype=torch.int64, device=dev)
+    token_pairs = torch.empty((tokens, k), dtype=torch.int32, device=dev)
+    rc = _lib.load().qq_moe_route_plan(experts.data_ptr(), weights.data_ptr(), tokens, k, num_experts,
+                                       pair_token.data_ptr(), pair_weight.data_ptr(), offsets.data_ptr(),
+                                       token_pairs.data_ptr(), err_ptr, stream_of(dev))
+    check(rc, "moe route plan")
+    return pair_token, pair_weight, offsets, token_pairs
 
 
 class B200SparseMoeBlock(_reference_block_class()):
@@ -120,17 +144,22 @@ class B200SparseMoeBlock(_reference_block_class()):
         x = x.contiguous()
         tg, tu, td, _, hidden, inter, num_experts = self._state(dev)
         tokens = x.shape[0]
-        pair_token, pair_weight, offsets, token_pairs = moe_plan(experts, weights.to(torch.bfloat16), num_experts)
+        weights = weights.to(torch.bfloat16)
+        if self._err_dev is None:
+            from qwenquest_b200.hisparse import host_device_pointer
+
+            self._err_dev = host_device_pointer(self._err)
+        if tokens * self.top_k <= ROUTE_PLAN_MAX_PAIRS:
+            pair_token, pair_weight, offsets, token_pairs = device_moe_plan(experts, weights, num_experts,
+                                                                             self._err_dev)
+        else:
+            pair_token, pair_weight, offsets, token_pairs = moe_plan(experts, weights, num_experts)
         pairs = pair_token.numel()
         h = torch.empty((pairs, inter), dtype=torch.bfloat16, device=dev)
         y = torch.empty((pairs, hidden), dtype=torch.bfloat16, device=dev)
         out = torch.empty_like(x)
         plan = _lib.QQMoePlan(pair_token.data_ptr(), offsets.data_ptr(), pair_weight.data_ptr(),
                               token_pairs.data_ptr(), tokens, pairs, self.top_k, num_experts)
-        if self._err_dev is None:
-            from qwenquest_b200.hisparse import host_device_pointer
-
-            self._err_dev = host_device_pointer(self._err)
         rc = lib.qq_moe_experts(plan, x.data_ptr(), x.stride(0), hidden, inter, tg.data_ptr(), tu.data_ptr(),
                                 td.data_ptr(), h.data_ptr(), y.data_ptr(), out.data_ptr(), out.stride(0),
                                 self._err_dev, stream_of(dev))

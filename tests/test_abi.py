@@ -122,6 +122,11 @@ def test_prefill_attention_and_moe_argument_errors_without_a_device(lib):
     assert moe(inter=700) == uns                                    # intermediate a multiple of 128
     assert moe(p=_lib.QQMoePlan(0x1000, 0x2000, 0x3000, 0x4000, 8, 64, 17, 128)) == uns  # top_k <= 16
     assert moe(x=0x10008) == uns
+    route = lib.qq_moe_route_plan
+    assert route(None, 0x1000, 8, 8, 128, 0x2000, 0x3000, 0x4000, 0x5000, None, None) == inv
+    assert route(0x1000, 0x1000, 8, 0, 128, 0x2000, 0x3000, 0x4000, 0x5000, None, None) == inv
+    assert route(0x1000, 0x1000, 257, 8, 128, 0x2000, 0x3000, 0x4000, 0x5000, None, None) == uns  # > 2048 pairs
+    assert route(0x1000, 0x1000, 8, 8, 2000, 0x2000, 0x3000, 0x4000, 0x5000, None, None) == uns  # > 1024 experts
 
 
 def test_device_error_bits_map_to_reference_exceptions():

@@ -111,3 +111,17 @@ def test_forward_makes_no_host_sync():
             torch.cuda.set_sync_debug_mode(0)
         ref = blk(x)
     assert float((out.float() - ref.float()).abs().max()) <= _tol(ref)
+
+
+@pytest.mark.parametrize("tokens", [1, 8, 200, 256])
+def test_device_plan_equals_torch_plan(tokens):
+    from qwenquest_b200.moe import device_moe_plan
+
+    g = torch.Generator(device="cuda").manual_seed(tokens)
+    logits = torch.randn(tokens, 128, generator=g, device="cuda")
+    weights, experts = torch.topk(torch.softmax(logits, -1), 8, dim=-1)
+    weights = weights.to(torch.bfloat16)
+    got = device_moe_plan(experts, weights, 128)
+    want = moe_plan(experts, weights, 128)
+    for a, b in zip(got, want, strict=True):
+        assert torch.equal(a.view(-1).to(b.dtype), b.view(-1)), (a, b)
