@@ -112,3 +112,26 @@ def test_fused_prefill_write_only_for_geometries_the_kernel_takes(dtype, kv, d, 
     assert be._extend_fusable() is fusable
     be.fused_extend = False
     assert be._extend_fusable() is False
+
+
+def test_prefill_attention_kernel_gate():
+    """Only bf16 pools of head_dim 128 with query heads in pairs of one KV group take
+    qq_extend_attention; other geometries (the reference's fp32 test models) keep its loop."""
+    be = _bare_backend()
+    be.fused_prefill_attention = True
+    plan = be._extend_plan(_batch([0, 1], [0, 64], [300, 5]))
+    assert plan.num_tiles == 3 + 1
+    # most key tiles first (3, 2, 1, 1); ties to the lower batch entry
+    assert plan.tiles_dev().tolist() == [(0 << 16) | 2, (0 << 16) | 1, (0 << 16) | 0, (1 << 16) | 0]
+
+    def fits(q_shape, q_dtype, kv_shape, kv_dtype):
+        q = torch.zeros(q_shape, dtype=q_dtype)
+        kv = torch.zeros(kv_shape, dtype=kv_dtype)
+        return be._prefill_kernel_fits(q, kv, plan)
+
+    assert fits((8, 32, 128), torch.bfloat16, (100, 4, 128), torch.bfloat16)
+    assert not fits((8, 32, 128), torch.float32, (100, 4, 128), torch.float32)   # fp32
+    assert not fits((8, 8, 64), torch.bfloat16, (100, 2, 64), torch.bfloat16)    # head_dim 64
+    assert not fits((8, 12, 128), torch.bfloat16, (100, 4, 128), torch.bfloat16)  # 3 query heads per KV head
+    be.fused_prefill_attention = False
+    assert not fits((8, 32, 128), torch.bfloat16, (100, 4, 128), torch.bfloat16)
