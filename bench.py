@@ -968,12 +968,11 @@ def config4_case(args) -> None:
     box = None
     if world > 1:
         # the box: every rank decoded its own shard; tokens summed, time of the slowest rank
-        t = torch.tensor([phase["decode"], phase["prefill"], -float(decode_tokens)], dtype=torch.float64, device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        n = torch.tensor([float(decode_tokens)], dtype=torch.float64, device=dev)
-        torch.distributed.all_reduce(n)
-        box = {"ranks": world, "decode_tokens": float(n[0]), "decode_s_max": float(t[0]),
-               "prefill_s_max": float(t[1]), "decode_tokens_per_s": float(n[0]) / float(t[0])}
+        from qwenquest_b200.sharding import box_totals
+
+        (dec_max, pre_max), (n_tok,) = box_totals([phase["decode"], phase["prefill"]], [decode_tokens], dev)
+        box = {"ranks": world, "decode_tokens": n_tok, "decode_s_max": dec_max, "prefill_s_max": pre_max,
+               "decode_tokens_per_s": n_tok / dec_max}
         if rank != 0:
             return
     replaced = "the attention backend and the MoE blocks" if moe_blocks else "the attention backend only"

@@ -74,3 +74,15 @@ def max_over_ranks(values: Sequence[float], device: torch.device | str = "cpu") 
     if torch.distributed.is_available() and torch.distributed.is_initialized():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return [float(x) for x in t.cpu()]
+
+
+def box_totals(times: Sequence[float], counts: Sequence[float], device: torch.device | str = "cpu"
+               ) -> tuple[list[float], list[float]]:
+    """The box's view of per-rank shards: each of ``times`` as its maximum over the ranks
+    (the slowest GPU sets the box's time) and each of ``counts`` summed over the ranks
+    (the tokens all shards produced).  Identity without a process group."""
+    slowest = max_over_ranks(times, device)
+    t = torch.tensor([float(c) for c in counts], dtype=torch.float64, device=device)
+    if torch.distributed.is_available() and torch.distributed.is_initialized():
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+    return slowest, [float(x) for x in t.cpu()]

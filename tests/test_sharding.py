@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from qwenquest_b200.sharding import max_over_ranks, request_layer_bytes, shard_requests
+from qwenquest_b200.sharding import box_totals, max_over_ranks, request_layer_bytes, shard_requests
 
 # benchmark config 2's shape: long ragged requests and two dense-fallback ones
 RAGGED = [70001, 98765, 131000, 65601, 120003, 77777, 101010, 88888, 66666, 130001, 99999, 75000,
@@ -84,6 +84,26 @@ def test_two_ranks_shard_and_take_the_slowest(tmp_path):
     assert sorted(i for s in shards for i in s) == list(range(len(RAGGED)))
     loads = [sum(request_layer_bytes(RAGGED[i]) for i in s) for s in shards]
     assert res["slowest"] == [float(max(loads)), float(world - 1)]
+
+
+def _box_rank_main(rank: int, world: int, port: int, out: str) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        # config 4's box: each rank decodes its shard in its own time with its own token count
+        res = box_totals([10.0 + rank, 3.0 - rank], [100.0 * (rank + 1)])
+        if rank == 0:
+            torch.save(res, out)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_box_totals(tmp_path):
+    out = str(tmp_path / "box.pt")
+    mp.spawn(_box_rank_main, args=(2, _free_port(), out), nprocs=2, join=True)
+    slowest, totals = torch.load(out)
+    assert slowest == [11.0, 3.0] and totals == [300.0]
 
 
 def test_max_over_ranks_without_a_group_is_the_identity():
